@@ -1,0 +1,308 @@
+#!/usr/bin/env python3
+"""Benchmark of the batched programmable bootstrap (PBS/s) on B200.
+
+Workload: the PBS microbenchmark -- a batch of 4096 LWE ciphertexts under
+n=834, k=1, N=2048, PBS gadget (2^23, 1), keyswitch gadget (2^3, 5), Gaussian noise at the
+set's std, uniform 4-bit messages (2 message + 2 carry bits) and a random 16-entry LUT.  One
+step = keyswitch + blind rotation + sample extraction of the whole batch (the work the
+reference does with one shortint apply_lookup_table call per ciphertext,
+runtime/src/ops/activation.rs:115).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
+
+N > 1 runs one process per GPU under torchrun; each rank bootstraps its own batch against
+its own key replica (weak scaling, no data-path collective), time = max over ranks.
+`--impl reference` times the CPU restatement of the same PBS (the oracle's f64 FFT path, the
+algorithm tfhe-rs runs on the CPU) on all host cores; it needs no GPU.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "penumbra-fhe_b200")
+
+SEED = 20241201
+FLOP_PER_PBS = 834 * (4 * 51200 + 32768)  # 1.981e8 FFT-equivalent FP64 flop (n=834, N=2048)
+WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussian noise, "
+            "uniform 4-bit messages, random 16-entry LUT")
+# DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts, from the ncu
+# capture summarised in profiles/blind_rotate_pbs4096.md (None until that capture exists).
+BR_TRAFFIC_PER_LAUNCH = None
+
+
+def load_package():
+    if "penumbra_b200" in sys.modules:
+        return sys.modules["penumbra_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "penumbra_b200", os.path.join(PKG_DIR, "__init__.py"),
+        submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["penumbra_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(
+                    ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                     "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                    timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self) -> dict:
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for name, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def cpu_reference_run(args, samples_per_step: int, warmup: int, steps: int):
+    """Time the oracle's f64-FFT PBS on all host cores; returns (PBS/s, info)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    threads = os.cpu_count() or 1
+    p = O.default_params()
+    keys = O.OracleKeys(p, SEED)
+    _ = keys.fbsk
+    rng = np.random.default_rng(SEED)
+    lut = rng.integers(0, 16, 16)
+    tv = keys.test_vector(lut)
+    msgs = rng.integers(0, 16, samples_per_step)
+    ct = keys.encrypt_big(msgs, seed=SEED + 1)
+    for _ in range(warmup):
+        keys.pbs_fft(ct, tv, threads=threads)
+    t0 = time.perf_counter()
+    out = None
+    for _ in range(steps):
+        out = keys.pbs_fft(ct, tv, threads=threads)
+    dt = time.perf_counter() - t0
+    ok = bool(np.array_equal(keys.decode(keys.phase_big(out)), lut[msgs]))
+    return samples_per_step * steps / dt, {"threads": threads, "decrypt_ok": ok,
+                                           "seconds": dt}
+
+
+def run_reference(args):
+    world, rank, _ = dist_setup(args)
+    if rank != 0:
+        return 0
+    steps, warm = args.steps, max(1, min(args.warmup, 1))
+    per_step = args.ref_samples
+    v, info = cpu_reference_run(args, per_step, warm, steps)
+    line = {
+        "impl": "reference", "metric": "pbs_per_second", "value": v, "unit": "PBS/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": warm,
+        "ms_per_step": 1e3 * per_step / v, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "batch": per_step,
+                   "note": "each step bootstraps a bounded sample of the 4096-ciphertext batch"},
+        "cpu_baseline": {"value": v, "unit": "PBS/s", "cores": info["threads"], "kind": "port",
+                         "sample": f"{per_step} PBS per step x {steps} steps on "
+                                   f"{info['threads']} host threads (oracle f64-FFT PBS)"},
+        "e2e": {"value": v, "unit": "PBS/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "decrypt_ok": info["decrypt_ok"],
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_gpu(args):
+    import numpy as np
+    import torch
+    world, rank, local = dist_setup(args)
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+    pnb = load_package()
+    B = args.batch
+    keys = pnb.keygen(seed=SEED, device=local)  # identical replica on every rank
+    rng = np.random.default_rng(SEED + rank)
+    lut = rng.integers(0, 16, 16)
+    msgs = rng.integers(0, 16, B)
+    tv = pnb.test_vector(keys, lut)
+    ct = pnb.encrypt(keys, torch.tensor(msgs), seed=SEED + 1 + rank)
+    out = torch.empty_like(ct)
+    small = torch.empty((B, keys.params.n + 1), dtype=torch.int64, device=dev)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # warm-up (also verifies the result decrypts to the LUT)
+    for _ in range(max(args.warmup, 0)):
+        pnb.pbs_batch(keys, tv, ct, out=out, workspace=small)
+    torch.cuda.synchronize(dev)
+    dec = pnb.decrypt_vec(keys, out).cpu().numpy()
+    decrypt_ok = bool(np.array_equal(dec, lut[msgs]))
+
+    # timed region: K steps, L2 flushed between steps (outside the step events)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            e0, e1, e2 = ev[i]
+            e0.record(stream)
+            pnb.keyswitch(keys, ct, out=small)
+            e1.record(stream)
+            pnb.blind_rotate(keys, tv, small, out=out)
+            e2.record(stream)
+        barrier()
+    step_ms = [a.elapsed_time(c) for a, b, c in ev]
+    br_ms = [b.elapsed_time(c) for a, b, c in ev]
+    ks_ms = [a.elapsed_time(b) for a, b, c in ev]
+    total_ms = sum(step_ms)
+    if dist is not None:
+        t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    value = world * B * args.steps / (total_ms * 1e-3)
+
+    # end-to-end: host ciphertexts in pinned memory -> device -> PBS -> host, every step
+    h_in = ct.cpu().pin_memory()
+    h_out = torch.empty_like(h_in).pin_memory()
+    d_in = torch.empty_like(ct)
+    barrier()
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for _ in range(args.steps):
+        d_in.copy_(h_in, non_blocking=True)
+        pnb.pbs_batch(keys, tv, d_in, out=out, workspace=small)
+        h_out.copy_(out, non_blocking=True)
+    e_end.record(stream)
+    barrier()
+    e2e_ms = e_start.elapsed_time(e_end)
+    if dist is not None:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_ok = bool(np.array_equal(pnb.decrypt_vec(keys, h_out.to(dev)).cpu().numpy(),
+                                 lut[msgs]))
+    e2e_value = world * B * args.steps / (e2e_ms * 1e-3)
+
+    # roofline of the dominant kernel (blind rotation): FP64-bound
+    peak = pnb.measure_fp64_peak(local)
+    br_avg = sum(br_ms) / len(br_ms)
+    achieved = FLOP_PER_PBS * B / (br_avg * 1e-3) / 1e12
+    roofline = {"bound": "fp64", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                "frac": achieved / peak,
+                "peak_source": "FP64 FMA probe measured in this run (no FP64 entry in "
+                               "MEASURED_PEAKS.json)",
+                "kernel": "blind_rotate_k1l1_kernel",
+                "traffic": BR_TRAFFIC_PER_LAUNCH}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        v, info = cpu_reference_run(args, args.ref_samples, 1, args.ref_steps)
+        cpu = {"value": v, "unit": "PBS/s", "cores": info["threads"], "kind": "port",
+               "sample": f"{args.ref_samples} PBS x {args.ref_steps} passes of the same "
+                         f"workload (oracle f64-FFT PBS, {info['threads']} host threads)"}
+
+    if dist is not None:
+        dist.barrier()
+    if rank == 0:
+        clocks = clk.summary()
+        line = {
+            "metric": "pbs_per_second", "value": value, "unit": "PBS/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": total_ms / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
+                       "parallelism": f"replicas{world}",
+                       "l2": "flushed (256 MB write) between timed steps"},
+            "e2e": {"value": e2e_value, "unit": "PBS/s",
+                    "h2d_bytes_per_step": int(h_in.numel() * 8),
+                    "d2h_bytes_per_step": int(h_out.numel() * 8)},
+            "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
+            "gpu_launches": 2 * args.steps,
+            "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
+            "decrypt_ok": decrypt_ok and e2e_ok,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=4096)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--ref-samples", type=int, default=1024)
+    ap.add_argument("--ref-steps", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,140 @@
+/*
+ * penumbra_b200.h -- C ABI of the B200 encrypted-evaluation library.
+ *
+ * The reference (Penumbra-FHE) evaluates an IR op graph on the CPU through the tfhe 1.6.3
+ * crate; it has no FFI of its own.  Each entry point below replaces one tfhe-rs call family the
+ * reference makes, so that an FFI shell over the reference runtime (a Rust `extern "C"` block,
+ * a ctypes stub) can route the same operations here.  Conventions:
+ *   - every function returns an int status (PNB_OK = 0); pnb_last_error() describes a failure;
+ *   - pointers named *_dev are device (HBM) pointers on the key set's device, *_host are host;
+ *   - ciphertexts are u64 words mod 2^64: an LWE ciphertext of dimension d is d+1 words with
+ *     the body last; batches are contiguous [count][d+1];
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); calls are asynchronous on it
+ *     unless documented otherwise and are thread-compatible (one stream per caller thread).
+ */
+#ifndef PENUMBRA_B200_H
+#define PENUMBRA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PNB_OK 0
+#define PNB_ERR_INVALID 1     /* bad argument / shape / parameter */
+#define PNB_ERR_CUDA 2        /* a CUDA runtime call failed */
+#define PNB_ERR_OOM 3         /* device allocation failed */
+#define PNB_ERR_TIMEOUT 4     /* a bounded device wait ran out */
+#define PNB_ERR_UNSUPPORTED 5 /* parameters outside the compiled kernel set */
+
+/* TFHE parameter set.  Field meaning follows tfhe-rs ClassicPBSParameters, which the reference
+ * pins as DEFAULT_PARAMS = PARAM_MESSAGE_2_CARRY_2_KS_PBS (runtime/src/keys.rs:29). */
+typedef struct pnb_params {
+  int32_t n;            /* small LWE dimension (keyswitch output / blind-rotation input) */
+  int32_t k;            /* GLWE dimension */
+  int32_t N;            /* polynomial size */
+  int32_t pbs_base_log; /* bootstrapping gadget: base 2^pbs_base_log ... */
+  int32_t pbs_level;    /* ... with pbs_level levels */
+  int32_t ks_base_log;  /* keyswitch gadget: base 2^ks_base_log ... */
+  int32_t ks_level;     /* ... with ks_level levels */
+  int32_t msg_bits;     /* message bits per block (reference MESSAGE_BITS = 2, keys.rs:36) */
+  int32_t carry_bits;   /* carry bits per block */
+  int32_t reserved;
+  double lwe_std;       /* small-key noise std as a fraction of the torus */
+  double glwe_std;      /* GLWE / big-key noise std as a fraction of the torus */
+} pnb_params;
+
+/* Opaque key set resident on one GPU: Fourier-domain bootstrapping key, keyswitching key and,
+ * for the client-side harness, the secret keys. */
+typedef struct pnb_keys pnb_keys;
+
+/* Library version (major*10000 + minor*100 + patch) and the last error of the calling thread. */
+int pnb_version(void);
+const char* pnb_last_error(void);
+
+/* Fill `out` with the library's default set: the Gaussian variant of
+ * PARAM_MESSAGE_2_CARRY_2_KS_PBS (n=834, k=1, N=2048, PBS 2^23 x 1, KS 2^3 x 5).
+ * Replaces: keys::DEFAULT_PARAMS (runtime/src/keys.rs:29). */
+int pnb_params_default(pnb_params* out);
+
+/* Generate secret keys, the bootstrapping key (then its Fourier form) and the keyswitching key
+ * on `device` from `seed`; blocks until the keys are resident.
+ * Replaces: keys::keygen -> tfhe gen_keys_radix (runtime/src/keys.rs:47-56). */
+int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** out);
+int pnb_keys_free(pnb_keys* keys);
+int pnb_keys_info(const pnb_keys* keys, pnb_params* params_out, int* device_out,
+                  size_t* fourier_bsk_bytes, size_t* ksk_bytes);
+/* Copy key material to host buffers (any pointer may be NULL): lwe_sk[n], glwe_sk[k*N],
+ * bsk[n*(k+1)*pbs_level*(k+1)*N] (standard domain), ksk[k*N*ks_level*(n+1)].  Blocking. */
+int pnb_keys_export(const pnb_keys* keys, uint64_t* lwe_sk_host, uint64_t* glwe_sk_host,
+                    uint64_t* bsk_host, uint64_t* ksk_host);
+
+/* Client side (test harness).  Encrypt messages[i]*delta under the big (k*N) key with GLWE
+ * noise; ciphertext i uses keystream index first_index+i of `seed`.
+ * Replaces: encrypt::encrypt -> RadixClientKey::encrypt_signed (runtime/src/encrypt.rs:20-22). */
+int pnb_encrypt_lwe(const pnb_keys* keys, const int64_t* messages_dev, uint64_t delta,
+                    uint64_t seed, uint64_t first_index, uint64_t* ct_dev, int count,
+                    void* stream);
+/* Phase b - <a, s> of each ciphertext under the big key (small_key = 0) or small key (1).
+ * Replaces the phase step of encrypt::decrypt_vec (runtime/src/encrypt.rs:43-45). */
+int pnb_phase_lwe(const pnb_keys* keys, const uint64_t* ct_dev, uint64_t* phase_dev, int count,
+                  int small_key, void* stream);
+
+/* Build the blind-rotation test vector (N words) of a lookup table: box m of width N/lut_len
+ * holds lut[m]*delta_out, rotated by half a box.
+ * Replaces: ServerKey::generate_lookup_table (runtime/src/ops/activation.rs:104,
+ * runtime/src/ops/requant.rs:193). */
+int pnb_test_vector(const pnb_keys* keys, const uint64_t* lut_host, int lut_len,
+                    uint64_t delta_out, uint64_t* tv_dev, void* stream);
+
+/* Keyswitch a batch of big-key LWE ciphertexts [count][k*N+1] to the small key [count][n+1]. */
+int pnb_keyswitch(const pnb_keys* keys, const uint64_t* in_dev, uint64_t* out_dev, int count,
+                  void* stream);
+
+/* Blind rotation + sample extraction of small-key ciphertexts [count][n+1] into big-key
+ * ciphertexts [count][k*N+1] (the second half of pnb_pbs_batch, without the keyswitch).
+ * Replaces: the programmable bootstrap inside shortint apply_lookup_table
+ * (runtime/src/ops/activation.rs:115). */
+int pnb_blind_rotate(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* small_dev,
+                     uint64_t* out_dev, int count, void* stream);
+
+/* Bytes of device scratch pnb_pbs_batch needs for `count` ciphertexts. */
+size_t pnb_pbs_workspace_bytes(const pnb_keys* keys, int count);
+
+/* Programmable bootstrap of a batch: keyswitch, modulus switch, blind rotation with the
+ * Fourier bootstrapping key, sample extraction.  in/out are [count][k*N+1] (may not alias).
+ * `workspace` (>= pnb_pbs_workspace_bytes) may be NULL, in which case the scratch is taken
+ * from the stream-ordered allocator for the duration of the call.
+ * Replaces: shortint ServerKey::apply_lookup_table (runtime/src/ops/activation.rs:115,
+ * runtime/src/ops/requant.rs:232), called once per ciphertext by the reference. */
+int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
+                  uint64_t* out_dev, int count, void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+/* Ciphertext x cleartext-weight contraction over LWE vectors mod 2^64:
+ *   Y[b][j][c] = sum_i W[j][i] * X[b][i][c]  + (c == lwe_len-1 ? bias[j]*delta : 0)
+ * W is int8 row-major [M][K], bias int64 [M] (may be NULL), X [batch][K][lwe_len],
+ * Y [batch][M][lwe_len].
+ * Replaces: the per-row scalar_mul_parallelized / add_parallelized / scalar_add_parallelized
+ * loops of Linear::eval (runtime/src/ops/linear.rs:52-75) and Conv2d::eval after im2col
+ * (runtime/src/ops/conv2d.rs:91-139). */
+int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M, int K,
+                     const uint64_t* X_dev, uint64_t* Y_dev, int batch, int lwe_len,
+                     void* stream);
+
+/* Negacyclic products out[c] = a[c] * b[c] mod (X^N + 1) through the same f64 FFT the blind
+ * rotation uses (a: small signed integers, |a| < 2^31; b: u64 torus), count polynomials.
+ * Diagnostic entry point for the FFT's precision; no reference counterpart. */
+int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64_t* b_dev,
+                           uint64_t* out_dev, int count, void* stream);
+
+/* Measure this device's FP64 FMA throughput (TFLOP/s) with a short register-only kernel; the
+ * roofline denominator of the blind rotation.  No reference counterpart. */
+int pnb_measure_fp64_peak(int device, double* tflops_out);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PENUMBRA_B200_H */

@@ -1,0 +1,337 @@
+"""penumbra_b200 -- Python host binding of the B200 encrypted-evaluation library.
+
+Every call goes through the C ABI of ``libpenumbra_b200.so`` (``include/penumbra_b200.h``);
+PyTorch only supplies device memory and the current CUDA stream.  There is no CPU fallback:
+importing this package without the built library raises.
+
+The names mirror the reference runtime's public surface (``runtime/src/lib.rs:36-45``):
+``keygen`` (``keys.rs:47``), ``encrypt`` / ``decrypt_vec`` (``encrypt.rs:20-45``), and the
+per-op kernels that replace tfhe-rs calls inside ``Linear``/``Conv2d``/``Requant``/``Activation``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import torch
+
+__all__ = [
+    "Params", "default_params", "KeySet", "keygen", "lib", "LibraryError",
+    "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "pbs_batch", "blind_rotate",
+    "pbs_workspace_bytes", "lwe_contract", "fft_negacyclic_mul", "measure_fp64_peak",
+]
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libpenumbra_b200.so")
+
+
+class LibraryError(RuntimeError):
+    """A C-ABI call returned a non-zero status."""
+
+    def __init__(self, fn: str, code: int, msg: str):
+        super().__init__(f"{fn} failed with status {code}: {msg}")
+        self.code = code
+
+
+class Params(C.Structure):
+    """``pnb_params`` (field meaning of tfhe-rs ClassicPBSParameters)."""
+    _fields_ = [
+        ("n", C.c_int32), ("k", C.c_int32), ("N", C.c_int32),
+        ("pbs_base_log", C.c_int32), ("pbs_level", C.c_int32),
+        ("ks_base_log", C.c_int32), ("ks_level", C.c_int32),
+        ("msg_bits", C.c_int32), ("carry_bits", C.c_int32), ("reserved", C.c_int32),
+        ("lwe_std", C.c_double), ("glwe_std", C.c_double),
+    ]
+
+    def delta(self) -> int:
+        """Plaintext scaling: one padding bit above msg_bits + carry_bits."""
+        return 1 << (63 - self.msg_bits - self.carry_bits)
+
+    def as_tuple(self):
+        return tuple(getattr(self, f) for f, _ in self._fields_)
+
+
+_SIGS = {
+    "pnb_version": (C.c_int, []),
+    "pnb_last_error": (C.c_char_p, []),
+    "pnb_params_default": (C.c_int, [C.POINTER(Params)]),
+    "pnb_keygen": (C.c_int, [C.c_int, C.POINTER(Params), C.c_uint64, C.POINTER(C.c_void_p)]),
+    "pnb_keys_free": (C.c_int, [C.c_void_p]),
+    "pnb_keys_info": (C.c_int, [C.c_void_p, C.POINTER(Params), C.POINTER(C.c_int),
+                                C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
+    "pnb_keys_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "pnb_encrypt_lwe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint64,
+                                  C.c_void_p, C.c_int, C.c_void_p]),
+    "pnb_phase_lwe": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                C.c_void_p]),
+    "pnb_test_vector": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_uint64, C.c_void_p,
+                                  C.c_void_p]),
+    "pnb_keyswitch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "pnb_blind_rotate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_void_p]),
+    "pnb_pbs_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
+    "pnb_pbs_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                C.c_void_p, C.c_size_t, C.c_void_p]),
+    "pnb_lwe_contract": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
+                                   C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
+                                         C.c_int, C.c_void_p]),
+    "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
+}
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    """Load ``libpenumbra_b200.so``; raise if it has not been built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(
+                f"{LIB_PATH} is missing: build it with `make -C {_HERE}` (or "
+                "__graft_entry__.build()); there is no CPU fallback")
+        L = C.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name)
+            f.restype = res
+            f.argtypes = args
+        _LIB = L
+    return _LIB
+
+
+def _check(fn: str, rc: int):
+    if rc != 0:
+        msg = lib().pnb_last_error().decode(errors="replace")
+        raise LibraryError(fn, rc, msg)
+
+
+def _stream(device) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _ptr(t: torch.Tensor | None) -> C.c_void_p:
+    if t is None:
+        return C.c_void_p(0)
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return C.c_void_p(t.data_ptr())
+
+
+def default_params() -> Params:
+    p = Params()
+    _check("pnb_params_default", lib().pnb_params_default(C.byref(p)))
+    return p
+
+
+class KeySet:
+    """Keys resident on one GPU (``pnb_keys``): Fourier BSK, KSK and client secrets."""
+
+    def __init__(self, handle: C.c_void_p, params: Params, device: int, seed: int):
+        self._h = handle
+        self.params = params
+        self.device = device
+        self.seed = seed
+
+    @property
+    def handle(self) -> C.c_void_p:
+        if not self._h:
+            raise ValueError("key set has been freed")
+        return self._h
+
+    def free(self):
+        if self._h:
+            lib().pnb_keys_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:  # interpreter shutdown
+            pass
+
+    @property
+    def big_dim(self) -> int:
+        return self.params.k * self.params.N
+
+    def info(self) -> dict:
+        p = Params()
+        dev = C.c_int()
+        fb = C.c_size_t()
+        kb = C.c_size_t()
+        _check("pnb_keys_info",
+               lib().pnb_keys_info(self.handle, C.byref(p), C.byref(dev), C.byref(fb),
+                                   C.byref(kb)))
+        return {"device": dev.value, "fourier_bsk_bytes": fb.value, "ksk_bytes": kb.value}
+
+    def export(self, lwe_sk=True, glwe_sk=True, bsk=False, ksk=False) -> dict:
+        """Copy key material to host numpy arrays (blocking)."""
+        import numpy as np
+        p = self.params
+        rows = (p.k + 1) * p.pbs_level
+        out = {}
+        bufs = []
+        for name, want, size in (
+                ("lwe_sk", lwe_sk, p.n), ("glwe_sk", glwe_sk, p.k * p.N),
+                ("bsk", bsk, p.n * rows * (p.k + 1) * p.N),
+                ("ksk", ksk, p.k * p.N * p.ks_level * (p.n + 1))):
+            if want:
+                a = np.zeros(size, dtype=np.uint64)
+                out[name] = a
+                bufs.append(C.c_void_p(a.ctypes.data))
+            else:
+                bufs.append(C.c_void_p(0))
+        _check("pnb_keys_export", lib().pnb_keys_export(self.handle, *bufs))
+        return out
+
+
+def keygen(params: Params | None = None, seed: int = 0, device: int = 0) -> KeySet:
+    """Generate keys on ``device`` (blocking).  Mirrors ``keys::keygen`` (keys.rs:47)."""
+    params = default_params() if params is None else params
+    h = C.c_void_p()
+    _check("pnb_keygen", lib().pnb_keygen(device, C.byref(params), seed, C.byref(h)))
+    return KeySet(h, params, device, seed)
+
+
+def _u64(t: torch.Tensor) -> torch.Tensor:
+    """View an int64 tensor as the u64 words the C ABI expects (torch has no uint64 math)."""
+    if t.dtype not in (torch.int64, torch.uint64):
+        raise TypeError(f"expected a 64-bit tensor, got {t.dtype}")
+    return t
+
+
+def encrypt(keys: KeySet, messages: torch.Tensor, seed: int, first_index: int = 0,
+            delta: int | None = None) -> torch.Tensor:
+    """LWE-encrypt ``messages * delta`` under the big key; returns [count, k*N+1] int64."""
+    dev = torch.device("cuda", keys.device)
+    msg = messages.to(device=dev, dtype=torch.int64).contiguous()
+    count = msg.numel()
+    ct = torch.empty((count, keys.big_dim + 1), dtype=torch.int64, device=dev)
+    delta = keys.params.delta() if delta is None else delta
+    _check("pnb_encrypt_lwe",
+           lib().pnb_encrypt_lwe(keys.handle, _ptr(msg), delta % (1 << 64), seed, first_index,
+                                 _ptr(ct), count, _stream(dev)))
+    return ct
+
+
+def phase(keys: KeySet, ct: torch.Tensor, small_key: bool = False) -> torch.Tensor:
+    """Phase ``b - <a, s>`` of each ciphertext (int64 view of the u64 torus value)."""
+    ct = _u64(ct).contiguous()
+    dim = keys.params.n if small_key else keys.big_dim
+    count = ct.numel() // (dim + 1)
+    out = torch.empty(count, dtype=torch.int64, device=ct.device)
+    _check("pnb_phase_lwe",
+           lib().pnb_phase_lwe(keys.handle, _ptr(ct), _ptr(out), count, int(small_key),
+                               _stream(ct.device)))
+    return out
+
+
+def decode(params: Params, phases: torch.Tensor, delta: int | None = None,
+           space: int | None = None) -> torch.Tensor:
+    """Round phases to the nearest multiple of ``delta`` and reduce modulo ``space``."""
+    delta = params.delta() if delta is None else delta
+    space = (2 << (params.msg_bits + params.carry_bits)) if space is None else space
+    shift = delta.bit_length() - 1
+    assert delta == 1 << shift, "delta must be a power of two"
+    ph = phases.to(torch.int64)
+    # round(phase / delta) with wrapping u64 arithmetic expressed in int64
+    r = torch.bitwise_right_shift(ph + (1 << (shift - 1)), shift)
+    return torch.remainder(r, space)
+
+
+def decrypt_vec(keys: KeySet, ct: torch.Tensor, delta: int | None = None,
+                space: int | None = None) -> torch.Tensor:
+    """Decrypt to integers.  Mirrors ``encrypt::decrypt_vec`` (encrypt.rs:43-45)."""
+    return decode(keys.params, phase(keys, ct), delta, space)
+
+
+def test_vector(keys: KeySet, lut, delta_out: int | None = None) -> torch.Tensor:
+    """Blind-rotation test vector of ``lut`` (``generate_lookup_table``)."""
+    import numpy as np
+    dev = torch.device("cuda", keys.device)
+    lut_a = np.ascontiguousarray(np.asarray(lut, dtype=np.int64).astype(np.uint64))
+    tv = torch.empty(keys.params.N, dtype=torch.int64, device=dev)
+    delta_out = keys.params.delta() if delta_out is None else delta_out
+    _check("pnb_test_vector",
+           lib().pnb_test_vector(keys.handle, C.c_void_p(lut_a.ctypes.data), len(lut_a),
+                                 delta_out % (1 << 64), _ptr(tv), _stream(dev)))
+    return tv
+
+
+def keyswitch(keys: KeySet, ct: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Keyswitch big-key ciphertexts [count, k*N+1] to the small key [count, n+1]."""
+    ct = _u64(ct).contiguous()
+    count = ct.numel() // (keys.big_dim + 1)
+    if out is None:
+        out = torch.empty((count, keys.params.n + 1), dtype=torch.int64, device=ct.device)
+    _check("pnb_keyswitch",
+           lib().pnb_keyswitch(keys.handle, _ptr(ct), _ptr(out), count, _stream(ct.device)))
+    return out
+
+
+def blind_rotate(keys: KeySet, tv: torch.Tensor, small: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Blind rotation + sample extraction of small-key ciphertexts [count, n+1]."""
+    small = _u64(small).contiguous()
+    count = small.numel() // (keys.params.n + 1)
+    if out is None:
+        out = torch.empty((count, keys.big_dim + 1), dtype=torch.int64, device=small.device)
+    _check("pnb_blind_rotate",
+           lib().pnb_blind_rotate(keys.handle, _ptr(tv), _ptr(small), _ptr(out), count,
+                                  _stream(small.device)))
+    return out
+
+
+def pbs_workspace_bytes(keys: KeySet, count: int) -> int:
+    return int(lib().pnb_pbs_workspace_bytes(keys.handle, count))
+
+
+def pbs_batch(keys: KeySet, tv: torch.Tensor, ct: torch.Tensor,
+              out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Programmable bootstrap of every ciphertext (``apply_lookup_table`` batched)."""
+    ct = _u64(ct).contiguous()
+    count = ct.numel() // (keys.big_dim + 1)
+    if out is None:
+        out = torch.empty((count, keys.big_dim + 1), dtype=torch.int64, device=ct.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    _check("pnb_pbs_batch",
+           lib().pnb_pbs_batch(keys.handle, _ptr(tv), _ptr(ct), _ptr(out), count,
+                               _ptr(workspace), ws_bytes, _stream(ct.device)))
+    return out
+
+
+def lwe_contract(W: torch.Tensor, bias: torch.Tensor | None, delta: int, X: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """``Y[b, j, :] = sum_i W[j, i] X[b, i, :] + bias[j] * delta`` on the body (mod 2^64)."""
+    if W.dtype != torch.int8:
+        raise TypeError("W must be int8")
+    M, K = W.shape
+    B, K2, L = X.shape
+    if K2 != K:
+        raise ValueError(f"X has {K2} inputs, W expects {K}")
+    if out is None:
+        out = torch.empty((B, M, L), dtype=torch.int64, device=X.device)
+    bias_t = None if bias is None else bias.to(device=X.device, dtype=torch.int64).contiguous()
+    with torch.cuda.device(X.device):
+        _check("pnb_lwe_contract",
+               lib().pnb_lwe_contract(_ptr(W.contiguous()), _ptr(bias_t), delta % (1 << 64), M,
+                                      K, _ptr(_u64(X).contiguous()), _ptr(out), B, L,
+                                      _stream(X.device)))
+    return out
+
+
+def fft_negacyclic_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Negacyclic products through the blind rotation's f64 FFT (diagnostic)."""
+    count, N = a.shape
+    out = torch.empty_like(b)
+    _check("pnb_fft_negacyclic_mul",
+           lib().pnb_fft_negacyclic_mul(a.device.index or 0, N, _ptr(a.contiguous()),
+                                        _ptr(b.contiguous()), _ptr(out), count,
+                                        _stream(a.device)))
+    return out
+
+
+def measure_fp64_peak(device: int = 0) -> float:
+    v = C.c_double()
+    _check("pnb_measure_fp64_peak", lib().pnb_measure_fp64_peak(device, C.byref(v)))
+    return v.value

@@ -1,0 +1,145 @@
+// fft1024.cuh -- warp-level negacyclic FFT for polynomials of size N = 2048.
+//
+// A real polynomial a(X) mod X^N + 1 is folded into M = N/2 complex points
+//   y_j = a_j + i a_{j+M},   z_j = y_j * zeta^j,   zeta = exp(i pi / N),
+// whose M-point DFT evaluates a(X) at the M roots zeta^(1-4t) of X^N + 1 (those with
+// X^(N/2) = i); the conjugate roots follow from a being real.  Products of such transforms are
+// negacyclic products.  This is the same "folding" evaluation tfhe-rs performs with its f64
+// FFT (tfhe-fft 0.10.1), restated for one warp:
+//
+//   M = 1024 = 32 x 32 (four-step).  Lane l holds y_{l + 32 m} in register m.
+//   forward : twist by zeta^{32 m} (per register) -> in-register DFT32 over m (DIF, output
+//             bit-reversed) -> twiddle zeta^l W^{l k2} -> shared-memory transpose ->
+//             in-register DFT32 (DIF).  Result: lane l, register r holds
+//             Z[32 bitrev(r) + bitrev(l)]  (the "permuted spectrum" order).
+//   inverse : exactly the mirror (DIT stages with conjugate twiddles), taking the permuted
+//             spectrum back to y'_{l + 32 n} in lane l, register n, scaled by 1/M.
+//
+// No bit reversal is ever materialised: pointwise products happen in the permuted order, and
+// the Fourier bootstrapping key is produced by the same forward routine.
+#pragma once
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "fft_consts.cuh"
+
+namespace pnb {
+
+constexpr int FFT_R = 32;       // registers (complex) per lane
+constexpr int FFT_M = 1024;     // complex points per polynomial
+constexpr int FFT_N = 2048;     // polynomial size
+
+// Twiddle tables for one device (all in device global memory).
+struct FftTables {
+  double2* wf;   // [r*32 + l] = zeta^l * W^{l * bitrev(r)}         (forward, between steps)
+  double2* wi;   // [n*32 + l] = zeta^{-n} * W^{-n * bitrev(l)}       (inverse, between steps)
+  double2* twf;  // [m] = zeta^{32 m}                                 (forward pre-twist)
+  double2* twi;  // [n] = zeta^{-32 n} / M                            (inverse post-twist)
+};
+
+__device__ __forceinline__ double2 cmul(double2 a, double2 b) {
+  return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
+}
+__device__ __forceinline__ double2 cmul_conj(double2 a, double c, double s) {
+  // a * (c - i s)
+  return make_double2(fma(a.x, c, a.y * s), fma(a.y, c, -a.x * s));
+}
+__device__ __forceinline__ double2 cmul_cs(double2 a, double c, double s) {
+  // a * (c + i s)
+  return make_double2(fma(a.x, c, -a.y * s), fma(a.x, s, a.y * c));
+}
+
+// Forward DFT32, decimation in frequency: natural input, bit-reversed output.
+__device__ __forceinline__ void dft32_dif(double2 (&x)[FFT_R]) {
+#pragma unroll
+  for (int len = 32; len >= 2; len >>= 1) {
+    const int half = len >> 1;
+#pragma unroll
+    for (int s = 0; s < 32; s += len) {
+#pragma unroll
+      for (int j = 0; j < half; ++j) {
+        double2 u = x[s + j], v = x[s + j + half];
+        x[s + j] = make_double2(u.x + v.x, u.y + v.y);
+        double2 d = make_double2(u.x - v.x, u.y - v.y);
+        const int k = j * (32 / len);  // W_len^j = W32^k
+        if (k == 0) {
+          x[s + j + half] = d;
+        } else if (k == 8) {  // -i
+          x[s + j + half] = make_double2(d.y, -d.x);
+        } else {
+          double c, sn;
+          w32(k, c, sn);
+          x[s + j + half] = cmul_cs(d, c, sn);
+        }
+      }
+    }
+  }
+}
+
+// Inverse DFT32 (exponent +), decimation in time: bit-reversed input, natural output. Unscaled.
+__device__ __forceinline__ void idft32_dit(double2 (&x)[FFT_R]) {
+#pragma unroll
+  for (int len = 2; len <= 32; len <<= 1) {
+    const int half = len >> 1;
+#pragma unroll
+    for (int s = 0; s < 32; s += len) {
+#pragma unroll
+      for (int j = 0; j < half; ++j) {
+        const int k = j * (32 / len);
+        double2 u = x[s + j], v = x[s + j + half];
+        double2 t;
+        if (k == 0) {
+          t = v;
+        } else if (k == 8) {  // conj(-i) = +i
+          t = make_double2(-v.y, v.x);
+        } else {
+          double c, sn;
+          w32(k, c, sn);
+          t = cmul_conj(v, c, sn);
+        }
+        x[s + j] = make_double2(u.x + t.x, u.y + t.y);
+        x[s + j + half] = make_double2(u.x - t.x, u.y - t.y);
+      }
+    }
+  }
+}
+
+// Swizzled 32x32 transpose through a per-warp shared buffer of 1024 double2.
+// Writes element (row = register index, col = lane) and reads back (row = lane, col = register).
+__device__ __forceinline__ void warp_transpose(double2 (&x)[FFT_R], double2* buf, int lane) {
+#pragma unroll
+  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r];
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 32; ++q) x[q] = buf[lane * 32 + ((q + lane) & 31)];
+  __syncwarp();
+}
+
+// Forward negacyclic FFT of one folded polynomial (see header comment).
+__device__ __forceinline__ void fft_forward(double2 (&x)[FFT_R], double2* buf, int lane,
+                                            const FftTables& tb) {
+#pragma unroll
+  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], tb.twf[m]);
+  dft32_dif(x);
+#pragma unroll
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], __ldg(&tb.wf[r * 32 + lane]));
+  warp_transpose(x, buf, lane);
+  dft32_dif(x);
+}
+
+// Inverse negacyclic FFT back to folded coefficients scaled by 1/M.
+__device__ __forceinline__ void fft_inverse(double2 (&x)[FFT_R], double2* buf, int lane,
+                                            const FftTables& tb) {
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.wi[n * 32 + lane]));
+  warp_transpose(x, buf, lane);
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], tb.twi[n]);
+}
+
+// Host: build (once per device) and fetch the tables of the current device.
+int fft_tables_get(FftTables* out);
+
+}  // namespace pnb

@@ -1,0 +1,44 @@
+// pnb_keys.h -- the opaque key set behind pnb_keys* and the internal launch entry points.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "../../include/penumbra_b200.h"
+
+struct pnb_keys {
+  int device;
+  pnb_params p;
+  uint64_t seed;
+  uint64_t* lwe_sk;    // [n]            small secret key (client side, harness only)
+  uint64_t* glwe_sk;   // [k*N]          GLWE secret key = big LWE key (client side)
+  uint64_t* bsk;       // [n][(k+1)l][k+1][N] standard-domain bootstrapping key
+  double2* fbsk;       // [n][(k+1)l][k+1][N/2] Fourier bootstrapping key (permuted spectrum)
+  uint64_t* ksk;       // [k*N][ks_level][n+1] keyswitching key
+  size_t bsk_words;
+  size_t fbsk_elems;
+  size_t ksk_words;
+};
+
+namespace pnb {
+int keygen_device(pnb_keys* K, cudaStream_t st);
+int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaStream_t st);
+int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,
+                     cudaStream_t st);
+int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
+                        uint64_t* out, int count, cudaStream_t st);
+size_t pbs_workspace_bytes(const pnb_keys* K, int count);
+int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
+              int count, void* ws, size_t ws_bytes, cudaStream_t st);
+int test_vector(const pnb_keys* K, const uint64_t* lut_host, int lut_len, uint64_t delta_out,
+                uint64_t* tv, cudaStream_t st);
+int fft_negacyclic_mul(int N, const int64_t* a, const uint64_t* b, uint64_t* out, int count,
+                       cudaStream_t st);
+int encrypt_lwe(const pnb_keys* K, const int64_t* msg, uint64_t delta, uint64_t seed,
+                uint64_t first, uint64_t* ct, int count, cudaStream_t st);
+int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count, int small,
+              cudaStream_t st);
+int lwe_contract(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                 const uint64_t* X, uint64_t* Y, int batch, int lwe_len, cudaStream_t st);
+int measure_fp64_peak(double* tflops);
+}  // namespace pnb

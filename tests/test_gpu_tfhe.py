@@ -1,0 +1,164 @@
+"""GPU parity of the TFHE kernels against the CPU oracle, through the C ABI.
+
+Bit-exact: secret keys, bootstrapping key, keyswitching key, client encryption, keyswitch.
+Decrypt-exact: programmable bootstrapping (the f64 FFT product makes output ciphertexts
+differ from the exact oracle's by fresh noise, as tfhe-rs's do, so parity is on decrypted
+values and on the noise level).  Golden values: runtime/tests/hello_fhe.rs:50-67.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SEED = 2024
+
+
+def _u64(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().numpy().view(np.uint64)
+
+
+@pytest.fixture(scope="module")
+def gkeys(pnb):
+    return pnb.keygen(seed=SEED, device=0)
+
+
+@pytest.fixture(scope="module")
+def okeys(oracle):
+    return oracle.OracleKeys(oracle.default_params(), seed=SEED)
+
+
+def test_keygen_bit_exact(gkeys, okeys):
+    ex = gkeys.export(lwe_sk=True, glwe_sk=True, bsk=True, ksk=True)
+    assert np.array_equal(ex["lwe_sk"], okeys.lwe_sk)
+    assert np.array_equal(ex["glwe_sk"], okeys.glwe_sk)
+    assert np.array_equal(ex["bsk"], okeys.bsk)
+    assert np.array_equal(ex["ksk"], okeys.ksk)
+
+
+def test_keygen_is_deterministic_per_seed(pnb, gkeys):
+    other = pnb.keygen(seed=SEED + 1, device=0)
+    a = gkeys.export(lwe_sk=True, glwe_sk=False)["lwe_sk"]
+    b = other.export(lwe_sk=True, glwe_sk=False)["lwe_sk"]
+    assert not np.array_equal(a, b)
+    again = pnb.keygen(seed=SEED, device=0)
+    assert np.array_equal(again.export(lwe_sk=False, glwe_sk=False, ksk=True)["ksk"],
+                          gkeys.export(lwe_sk=False, glwe_sk=False, ksk=True)["ksk"])
+
+
+def test_encrypt_bit_exact_and_decrypts(pnb, gkeys, okeys):
+    msgs = np.arange(16)
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=5)
+    assert np.array_equal(_u64(ct), okeys.encrypt_big(msgs, seed=5))
+    assert torch.equal(pnb.decrypt_vec(gkeys, ct).cpu(), torch.tensor(msgs))
+
+
+@pytest.mark.parametrize("count", [1, 33, 70])
+def test_keyswitch_bit_exact(pnb, gkeys, okeys, count):
+    rng = np.random.default_rng(count)
+    msgs = rng.integers(0, 16, count)
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=77)
+    ks = pnb.keyswitch(gkeys, ct)
+    assert np.array_equal(_u64(ks), okeys.keyswitch(_u64(ct)))
+    dec = okeys.decode(okeys.phase_small(_u64(ks)))
+    assert np.array_equal(dec, msgs)
+
+
+def test_fft_negacyclic_product_precision(pnb, oracle):
+    # Digits in the blind rotation's range (|d| < 2^22) times uniform torus polynomials.
+    rng = np.random.default_rng(9)
+    N, count = 2048, 4
+    a = rng.integers(-(1 << 22), 1 << 22, (count, N), dtype=np.int64)
+    b = rng.integers(0, 1 << 63, (count, N), dtype=np.uint64) * np.uint64(2) + \
+        rng.integers(0, 2, (count, N), dtype=np.uint64)
+    got = _u64(pnb.fft_negacyclic_mul(torch.tensor(a, device="cuda"),
+                                      torch.tensor(b.view(np.int64), device="cuda")))
+    import ctypes as C
+    L = oracle.lib()
+    u64p = C.POINTER(C.c_uint64)
+    worst = 0.0
+    for c in range(count):
+        ex = np.zeros(N, dtype=np.uint64)
+        av = np.ascontiguousarray(a[c].view(np.uint64))
+        bv = np.ascontiguousarray(b[c])
+        L.orc_negacyclic_mul(N, av.ctypes.data_as(u64p), bv.ctypes.data_as(u64p),
+                             ex.ctypes.data_as(u64p))
+        d = (got[c] - ex).view(np.int64).astype(np.float64)
+        worst = max(worst, float(np.abs(d).max()))
+    # f64 products of magnitude ~2^90 keep ~53 bits: the error stays below 2^46 of 2^64.
+    assert worst < 2.0 ** 46, f"worst FFT error 2^{np.log2(worst):.1f}"
+
+
+def _noise(phases: np.ndarray, want: np.ndarray, delta: int) -> np.ndarray:
+    return (phases - want.astype(np.uint64) * np.uint64(delta)).view(np.int64).astype(np.float64)
+
+
+def test_pbs_hello_fhe_golden(pnb, gkeys):
+    lut = [(v + 1) % 4 for v in range(4)] + [0] * 12
+    tv = pnb.test_vector(gkeys, lut)
+    ct = pnb.encrypt(gkeys, torch.arange(4), seed=21)
+    out = pnb.pbs_batch(gkeys, tv, ct)
+    assert pnb.decrypt_vec(gkeys, out).cpu().tolist() == [1, 2, 3, 0]
+
+
+def test_pbs_random_lut_batch_4096(pnb, gkeys, okeys):
+    rng = np.random.default_rng(12)
+    msgs = rng.integers(0, 16, 4096)
+    lut = rng.integers(0, 16, 16)
+    tv = pnb.test_vector(gkeys, lut)
+    assert np.array_equal(_u64(tv), okeys.test_vector(lut))
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=1)
+    out = pnb.pbs_batch(gkeys, tv, ct)
+    dec = pnb.decrypt_vec(gkeys, out).cpu().numpy()
+    assert np.array_equal(dec, lut[msgs])
+    # Noise level against the oracle's FFT bootstrap on the same keys and inputs.
+    gpu_noise = _noise(_u64(pnb.phase(gkeys, out)), lut[msgs], gkeys.params.delta())
+    sub = 256
+    ref = okeys.pbs_fft(_u64(ct[:sub]), okeys.test_vector(lut))
+    assert np.array_equal(okeys.decode(okeys.phase_big(ref)), lut[msgs[:sub]])
+    ref_noise = _noise(okeys.phase_big(ref), lut[msgs[:sub]], gkeys.params.delta())
+    ratio = gpu_noise.var() / ref_noise.var()
+    assert 0.6 < ratio < 1.5, f"noise variance ratio {ratio:.3f}"
+    assert np.abs(gpu_noise).max() < 2.0 ** 55
+
+
+def test_pbs_agrees_with_exact_oracle(pnb, gkeys, okeys):
+    rng = np.random.default_rng(13)
+    msgs = rng.integers(0, 16, 2)
+    lut = rng.integers(0, 16, 16)
+    tv = pnb.test_vector(gkeys, lut)
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=2)
+    out = _u64(pnb.pbs_batch(gkeys, tv, ct))
+    ex = okeys.pbs_exact(_u64(ct), okeys.test_vector(lut))
+    d = gkeys.params.delta()
+    assert np.array_equal(okeys.decode(okeys.phase_big(ex)), lut[msgs])
+    assert np.array_equal(okeys.decode(okeys.phase_big(out)), lut[msgs])
+    diff = (okeys.phase_big(out) - okeys.phase_big(ex)).view(np.int64).astype(np.float64)
+    assert np.all(np.abs(diff) < d / 8)
+
+
+def test_pbs_deterministic_and_workspace(pnb, gkeys):
+    rng = np.random.default_rng(14)
+    msgs = rng.integers(0, 16, 100)
+    tv = pnb.test_vector(gkeys, rng.integers(0, 16, 16))
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=3)
+    a = pnb.pbs_batch(gkeys, tv, ct)
+    ws = torch.empty(pnb.pbs_workspace_bytes(gkeys, 100), dtype=torch.uint8, device="cuda")
+    b = pnb.pbs_batch(gkeys, tv, ct, workspace=ws)
+    assert torch.equal(a, b)
+
+
+def test_pbs_argument_errors(pnb, gkeys):
+    tv = pnb.test_vector(gkeys, list(range(16)))
+    ct = pnb.encrypt(gkeys, torch.arange(4), seed=4)
+    empty = pnb.pbs_batch(gkeys, tv, ct[:0])
+    assert empty.shape[0] == 0
+    with pytest.raises(pnb.LibraryError):
+        pnb.pbs_batch(gkeys, tv, ct, out=ct)  # aliasing
+    small = torch.empty(8, dtype=torch.uint8, device="cuda")
+    with pytest.raises(pnb.LibraryError):
+        pnb.pbs_batch(gkeys, tv, ct, workspace=small)
+    with pytest.raises(pnb.LibraryError):
+        pnb.test_vector(gkeys, list(range(3)))  # does not divide N
