@@ -37,6 +37,14 @@ struct FftTables {
   double2* twi;  // [n] = zeta^{-32 n} / M                            (inverse post-twist)
 };
 
+// Read-only load the compiler may not hoist out of the blind-rotation loop: the twiddles are
+// loop-invariant, and keeping all of them in registers across iterations would spill.
+__device__ __forceinline__ double2 ld_tw(const double2* p) {
+  double2 v;
+  asm volatile("ld.global.nc.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
+  return v;
+}
+
 __device__ __forceinline__ double2 cmul(double2 a, double2 b) {
   return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
 }
@@ -49,59 +57,73 @@ __device__ __forceinline__ double2 cmul_cs(double2 a, double c, double s) {
   return make_double2(fma(a.x, c, -a.y * s), fma(a.x, s, a.y * c));
 }
 
-// Forward DFT32, decimation in frequency: natural input, bit-reversed output.
-__device__ __forceinline__ void dft32_dif(double2 (&x)[FFT_R]) {
+// One radix-2 stage of span LEN over the 32 registers.  Templated so that every register
+// index is a compile-time constant (a runtime stage length would demote x[] to local memory).
+template <int LEN>
+__device__ __forceinline__ void dif_stage(double2 (&x)[FFT_R]) {
+  constexpr int HALF = LEN / 2;
 #pragma unroll
-  for (int len = 32; len >= 2; len >>= 1) {
-    const int half = len >> 1;
+  for (int s = 0; s < 32; s += LEN) {
 #pragma unroll
-    for (int s = 0; s < 32; s += len) {
-#pragma unroll
-      for (int j = 0; j < half; ++j) {
-        double2 u = x[s + j], v = x[s + j + half];
-        x[s + j] = make_double2(u.x + v.x, u.y + v.y);
-        double2 d = make_double2(u.x - v.x, u.y - v.y);
-        const int k = j * (32 / len);  // W_len^j = W32^k
-        if (k == 0) {
-          x[s + j + half] = d;
-        } else if (k == 8) {  // -i
-          x[s + j + half] = make_double2(d.y, -d.x);
-        } else {
-          double c, sn;
-          w32(k, c, sn);
-          x[s + j + half] = cmul_cs(d, c, sn);
-        }
+    for (int j = 0; j < HALF; ++j) {
+      const double2 u = x[s + j], v = x[s + j + HALF];
+      x[s + j] = make_double2(u.x + v.x, u.y + v.y);
+      const double2 d = make_double2(u.x - v.x, u.y - v.y);
+      const int k = j * (32 / LEN);  // W_LEN^j = W32^k
+      if (k == 0) {
+        x[s + j + HALF] = d;
+      } else if (k == 8) {  // -i
+        x[s + j + HALF] = make_double2(d.y, -d.x);
+      } else {
+        double c, sn;
+        w32(k, c, sn);
+        x[s + j + HALF] = cmul_cs(d, c, sn);
       }
     }
   }
 }
 
-// Inverse DFT32 (exponent +), decimation in time: bit-reversed input, natural output. Unscaled.
-__device__ __forceinline__ void idft32_dit(double2 (&x)[FFT_R]) {
+template <int LEN>
+__device__ __forceinline__ void dit_stage_inv(double2 (&x)[FFT_R]) {
+  constexpr int HALF = LEN / 2;
 #pragma unroll
-  for (int len = 2; len <= 32; len <<= 1) {
-    const int half = len >> 1;
+  for (int s = 0; s < 32; s += LEN) {
 #pragma unroll
-    for (int s = 0; s < 32; s += len) {
-#pragma unroll
-      for (int j = 0; j < half; ++j) {
-        const int k = j * (32 / len);
-        double2 u = x[s + j], v = x[s + j + half];
-        double2 t;
-        if (k == 0) {
-          t = v;
-        } else if (k == 8) {  // conj(-i) = +i
-          t = make_double2(-v.y, v.x);
-        } else {
-          double c, sn;
-          w32(k, c, sn);
-          t = cmul_conj(v, c, sn);
-        }
-        x[s + j] = make_double2(u.x + t.x, u.y + t.y);
-        x[s + j + half] = make_double2(u.x - t.x, u.y - t.y);
+    for (int j = 0; j < HALF; ++j) {
+      const int k = j * (32 / LEN);
+      const double2 u = x[s + j], v = x[s + j + HALF];
+      double2 t;
+      if (k == 0) {
+        t = v;
+      } else if (k == 8) {  // conj(-i) = +i
+        t = make_double2(-v.y, v.x);
+      } else {
+        double c, sn;
+        w32(k, c, sn);
+        t = cmul_conj(v, c, sn);
       }
+      x[s + j] = make_double2(u.x + t.x, u.y + t.y);
+      x[s + j + HALF] = make_double2(u.x - t.x, u.y - t.y);
     }
   }
+}
+
+// Forward DFT32, decimation in frequency: natural input, bit-reversed output.
+__device__ __forceinline__ void dft32_dif(double2 (&x)[FFT_R]) {
+  dif_stage<32>(x);
+  dif_stage<16>(x);
+  dif_stage<8>(x);
+  dif_stage<4>(x);
+  dif_stage<2>(x);
+}
+
+// Inverse DFT32 (exponent +), decimation in time: bit-reversed input, natural output. Unscaled.
+__device__ __forceinline__ void idft32_dit(double2 (&x)[FFT_R]) {
+  dit_stage_inv<2>(x);
+  dit_stage_inv<4>(x);
+  dit_stage_inv<8>(x);
+  dit_stage_inv<16>(x);
+  dit_stage_inv<32>(x);
 }
 
 // Swizzled 32x32 transpose through a per-warp shared buffer of 1024 double2.
@@ -119,10 +141,10 @@ __device__ __forceinline__ void warp_transpose(double2 (&x)[FFT_R], double2* buf
 __device__ __forceinline__ void fft_forward(double2 (&x)[FFT_R], double2* buf, int lane,
                                             const FftTables& tb) {
 #pragma unroll
-  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], tb.twf[m]);
+  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], ld_tw(&tb.twf[m]));
   dft32_dif(x);
 #pragma unroll
-  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], __ldg(&tb.wf[r * 32 + lane]));
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], ld_tw(&tb.wf[r * 32 + lane]));
   warp_transpose(x, buf, lane);
   dft32_dif(x);
 }
@@ -132,11 +154,11 @@ __device__ __forceinline__ void fft_inverse(double2 (&x)[FFT_R], double2* buf, i
                                             const FftTables& tb) {
   idft32_dit(x);
 #pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.wi[n * 32 + lane]));
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], ld_tw(&tb.wi[n * 32 + lane]));
   warp_transpose(x, buf, lane);
   idft32_dit(x);
 #pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], tb.twi[n]);
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], ld_tw(&tb.twi[n]));
 }
 
 // Host: build (once per device) and fetch the tables of the current device.

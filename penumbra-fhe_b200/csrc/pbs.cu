@@ -257,6 +257,9 @@ __global__ void __launch_bounds__(64) blind_rotate_k1l1_kernel(
     double2 x[FFT_R];
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
+      // Keep the shared-memory loads of a few coefficients in flight at a time: hoisting all
+      // 64 of them ahead of the conversions would exceed the register budget.
+      if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
       const uint64_t v0 = rot_coef(my, j, a) - my[j];
       const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
@@ -277,6 +280,7 @@ __global__ void __launch_bounds__(64) blind_rotate_k1l1_kernel(
     const double2* f_oth = g + (size_t)((warp ^ 1) * 2 + warp) * FFT_M;
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
+      if ((r & 3) == 0) asm volatile("" ::: "memory");
       const int e = r * 32 + lane;
       const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
       const double2 dt = otherbuf[e];
@@ -288,6 +292,7 @@ __global__ void __launch_bounds__(64) blind_rotate_k1l1_kernel(
     fft_inverse(x, mybuf, lane, tb);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
+      if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
       my[j] += f64_to_torus(x[m].x);
       my[j + FFT_M] += f64_to_torus(x[m].y);
