@@ -182,6 +182,8 @@ def run_gpu(args):
     ct = pnb.encrypt(keys, torch.tensor(msgs), seed=SEED + 1 + rank)
     out = torch.empty_like(ct)
     small = torch.empty((B, keys.params.n + 1), dtype=torch.int64, device=dev)
+    ks_ws = torch.empty(pnb.keyswitch_workspace_bytes(keys, B), dtype=torch.uint8, device=dev)
+    pbs_ws = torch.empty(pnb.pbs_workspace_bytes(keys, B), dtype=torch.uint8, device=dev)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)  # > 126 MB L2
     stream = torch.cuda.current_stream(dev)
 
@@ -192,7 +194,7 @@ def run_gpu(args):
 
     # warm-up (also verifies the result decrypts to the LUT)
     for _ in range(max(args.warmup, 0)):
-        pnb.pbs_batch(keys, tv, ct, out=out, workspace=small)
+        pnb.pbs_batch(keys, tv, ct, out=out, workspace=pbs_ws)
     torch.cuda.synchronize(dev)
     dec = pnb.decrypt_vec(keys, out).cpu().numpy()
     decrypt_ok = bool(np.array_equal(dec, lut[msgs]))
@@ -206,7 +208,7 @@ def run_gpu(args):
             flush.zero_()
             e0, e1, e2 = ev[i]
             e0.record(stream)
-            pnb.keyswitch(keys, ct, out=small)
+            pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
             e1.record(stream)
             pnb.blind_rotate(keys, tv, small, out=out)
             e2.record(stream)
@@ -231,7 +233,7 @@ def run_gpu(args):
     e_start.record(stream)
     for _ in range(args.steps):
         d_in.copy_(h_in, non_blocking=True)
-        pnb.pbs_batch(keys, tv, d_in, out=out, workspace=small)
+        pnb.pbs_batch(keys, tv, d_in, out=out, workspace=pbs_ws)
         h_out.copy_(out, non_blocking=True)
     e_end.record(stream)
     barrier()
@@ -278,7 +280,7 @@ def run_gpu(args):
                     "h2d_bytes_per_step": int(h_in.numel() * 8),
                     "d2h_bytes_per_step": int(h_out.numel() * 8)},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": 3 * args.steps,
             "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
             "decrypt_ok": decrypt_ok and e2e_ok,
         }

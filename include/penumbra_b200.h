@@ -89,9 +89,14 @@ int pnb_phase_lwe(const pnb_keys* keys, const uint64_t* ct_dev, uint64_t* phase_
 int pnb_test_vector(const pnb_keys* keys, const uint64_t* lut_host, int lut_len,
                     uint64_t delta_out, uint64_t* tv_dev, void* stream);
 
-/* Keyswitch a batch of big-key LWE ciphertexts [count][k*N+1] to the small key [count][n+1]. */
+/* Keyswitch a batch of big-key LWE ciphertexts [count][k*N+1] to the small key [count][n+1],
+ * on the tensor cores.  `workspace` (>= pnb_keyswitch_workspace_bytes, 256-byte aligned) may be
+ * NULL, in which case the digit scratch comes from the stream-ordered allocator.
+ * Replaces: the keyswitch inside shortint apply_lookup_table (KS_PBS order,
+ * runtime/src/ops/activation.rs:115). */
+size_t pnb_keyswitch_workspace_bytes(const pnb_keys* keys, int count);
 int pnb_keyswitch(const pnb_keys* keys, const uint64_t* in_dev, uint64_t* out_dev, int count,
-                  void* stream);
+                  void* workspace, size_t workspace_bytes, void* stream);
 
 /* Blind rotation + sample extraction of small-key ciphertexts [count][n+1] into big-key
  * ciphertexts [count][k*N+1] (the second half of pnb_pbs_batch, without the keyswitch).
@@ -129,6 +134,10 @@ int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delt
  * Diagnostic entry point for the FFT's precision; no reference counterpart. */
 int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64_t* b_dev,
                            uint64_t* out_dev, int count, void* stream);
+
+/* Read and clear the device status word of the tensor-core kernels: 0 when no bounded wait ran
+ * out since the last read, non-zero (the waiting role) otherwise.  No reference counterpart. */
+int pnb_device_status(int device, int* status_out);
 
 /* Measure this device's FP64 FMA throughput (TFLOP/s) with a short register-only kernel; the
  * roofline denominator of the blind rotation.  No reference counterpart. */

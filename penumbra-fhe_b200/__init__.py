@@ -17,8 +17,10 @@ import torch
 
 __all__ = [
     "Params", "default_params", "KeySet", "keygen", "lib", "LibraryError",
-    "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "pbs_batch", "blind_rotate",
+    "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
+    "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "fft_negacyclic_mul", "measure_fp64_peak",
+    "device_status",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -66,7 +68,9 @@ _SIGS = {
                                 C.c_void_p]),
     "pnb_test_vector": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_uint64, C.c_void_p,
                                   C.c_void_p]),
-    "pnb_keyswitch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p]),
+    "pnb_keyswitch_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
+    "pnb_keyswitch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                C.c_size_t, C.c_void_p]),
     "pnb_blind_rotate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                    C.c_void_p]),
     "pnb_pbs_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
@@ -77,6 +81,7 @@ _SIGS = {
     "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_int, C.c_void_p]),
     "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
+    "pnb_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
 }
 
 _LIB = None
@@ -257,14 +262,21 @@ def test_vector(keys: KeySet, lut, delta_out: int | None = None) -> torch.Tensor
     return tv
 
 
-def keyswitch(keys: KeySet, ct: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+def keyswitch_workspace_bytes(keys: KeySet, count: int) -> int:
+    return int(lib().pnb_keyswitch_workspace_bytes(keys.handle, count))
+
+
+def keyswitch(keys: KeySet, ct: torch.Tensor, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Keyswitch big-key ciphertexts [count, k*N+1] to the small key [count, n+1]."""
     ct = _u64(ct).contiguous()
     count = ct.numel() // (keys.big_dim + 1)
     if out is None:
         out = torch.empty((count, keys.params.n + 1), dtype=torch.int64, device=ct.device)
+    ws_bytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     _check("pnb_keyswitch",
-           lib().pnb_keyswitch(keys.handle, _ptr(ct), _ptr(out), count, _stream(ct.device)))
+           lib().pnb_keyswitch(keys.handle, _ptr(ct), _ptr(out), count, _ptr(workspace),
+                               ws_bytes, _stream(ct.device)))
     return out
 
 
@@ -329,6 +341,13 @@ def fft_negacyclic_mul(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
                                         _ptr(b.contiguous()), _ptr(out), count,
                                         _stream(a.device)))
     return out
+
+
+def device_status(device: int = 0) -> int:
+    """Read and clear the tensor-core kernels' status word (0 = every bounded wait completed)."""
+    v = C.c_int()
+    _check("pnb_device_status", lib().pnb_device_status(device, C.byref(v)))
+    return v.value
 
 
 def measure_fp64_peak(device: int = 0) -> float:

@@ -115,7 +115,8 @@ int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** o
   const size_t rows = (size_t)(p.k + 1) * p.pbs_level;
   K->bsk_words = (size_t)p.n * rows * (p.k + 1) * p.N;
   K->fbsk_elems = K->bsk_words / 2;
-  K->ksk_words = (size_t)p.k * p.N * p.ks_level * (p.n + 1);
+  K->ksk_row = (p.n + 2) & ~1;
+  K->ksk_words = (size_t)p.k * p.N * p.ks_level * K->ksk_row;
   cudaError_t e;
   if ((e = cudaMalloc(&K->lwe_sk, sizeof(uint64_t) * p.n)) != cudaSuccess ||
       (e = cudaMalloc(&K->glwe_sk, sizeof(uint64_t) * p.k * p.N)) != cudaSuccess ||
@@ -174,7 +175,11 @@ int pnb_keys_export(const pnb_keys* K, uint64_t* lwe_sk, uint64_t* glwe_sk, uint
   if (glwe_sk)
     PNB_CUDA(cudaMemcpy(glwe_sk, K->glwe_sk, 8 * (size_t)p.k * p.N, cudaMemcpyDeviceToHost));
   if (bsk) PNB_CUDA(cudaMemcpy(bsk, K->bsk, 8 * K->bsk_words, cudaMemcpyDeviceToHost));
-  if (ksk) PNB_CUDA(cudaMemcpy(ksk, K->ksk, 8 * K->ksk_words, cudaMemcpyDeviceToHost));
+  if (ksk) {
+    const size_t rows = (size_t)p.k * p.N * p.ks_level;
+    PNB_CUDA(cudaMemcpy2D(ksk, 8 * (size_t)(p.n + 1), K->ksk, 8 * (size_t)K->ksk_row,
+                          8 * (size_t)(p.n + 1), rows, cudaMemcpyDeviceToHost));
+  }
   return PNB_OK;
 }
 
@@ -216,17 +221,28 @@ int pnb_test_vector(const pnb_keys* K, const uint64_t* lut_host, int lut_len,
   return test_vector(K, lut_host, lut_len, delta_out, tv_dev, (cudaStream_t)stream);
 }
 
+size_t pnb_keyswitch_workspace_bytes(const pnb_keys* K, int count) {
+  if (!K || count <= 0) return 0;
+  return ks_tc_workspace_bytes(K->p, count);
+}
+
 int pnb_keyswitch(const pnb_keys* K, const uint64_t* in_dev, uint64_t* out_dev, int count,
-                  void* stream) {
+                  void* workspace, size_t workspace_bytes, void* stream) {
   int rc = check_keys(K);
   if (rc) return rc;
   if (count < 0 || (count > 0 && (!in_dev || !out_dev))) {
     set_error("keyswitch: bad buffers or count %d", count);
     return PNB_ERR_INVALID;
   }
+  if (workspace && (workspace_bytes < ks_tc_workspace_bytes(K->p, count) ||
+                    (uintptr_t)workspace % 256 != 0)) {
+    set_error("keyswitch: workspace must be 256-byte aligned and hold %zu bytes (got %zu)",
+              ks_tc_workspace_bytes(K->p, count), workspace_bytes);
+    return PNB_ERR_INVALID;
+  }
   DeviceGuard g(K->device);
   if (g.rc) return g.rc;
-  return keyswitch_launch(K, in_dev, out_dev, count, (cudaStream_t)stream);
+  return keyswitch_launch(K, in_dev, out_dev, count, workspace, (cudaStream_t)stream);
 }
 
 int pnb_blind_rotate(const pnb_keys* K, const uint64_t* tv_dev, const uint64_t* small_dev,
@@ -285,6 +301,13 @@ int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64
   DeviceGuard g(device);
   if (g.rc) return g.rc;
   return fft_negacyclic_mul(N, a_dev, b_dev, out_dev, count, (cudaStream_t)stream);
+}
+
+int pnb_device_status(int device, int* status_out) {
+  if (!status_out) { set_error("status_out is NULL"); return PNB_ERR_INVALID; }
+  DeviceGuard g(device);
+  if (g.rc) return g.rc;
+  return tc_status_read_and_clear(status_out);
 }
 
 int pnb_measure_fp64_peak(int device, double* tflops_out) {

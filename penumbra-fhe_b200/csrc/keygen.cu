@@ -163,13 +163,14 @@ __global__ void __launch_bounds__(256) bsk_body_kernel(uint64_t* bsk, const int*
 
 // One block per keyswitching-key row (i, j): LWE encryption of S_big[i] * q / B^(j+1).
 __global__ void __launch_bounds__(128) ksk_kernel(uint64_t* ksk, const uint64_t* glwe_sk,
-                                                  const uint64_t* lwe_sk, int n, int level,
-                                                  int base_log, uint64_t seed,
+                                                  const uint64_t* lwe_sk, int n, int row_words,
+                                                  int level, int base_log, uint64_t seed,
                                                   double sigma_abs) {
   __shared__ uint64_t red[128];
   const size_t rowi = blockIdx.x;  // i * level + j
   const int i = (int)(rowi / level), j = (int)(rowi % level);
-  uint64_t* ct = ksk + rowi * (size_t)(n + 1);
+  uint64_t* ct = ksk + rowi * (size_t)row_words;
+  for (int t = n + 1 + threadIdx.x; t < row_words; t += 128) ct[t] = 0;  // row padding
   uint64_t part = 0;
   for (int t = threadIdx.x; t < n; t += 128) {
     const uint64_t a = rand_word(seed, DOM_KSK_MASK, rowi * n + t);
@@ -243,8 +244,9 @@ int keygen_device(pnb_keys* K, cudaStream_t st) {
                                                  p.pbs_base_log);
   PNB_CHECK_LAUNCH("bsk_body_kernel");
   PNB_CUDA(cudaFreeAsync(ones, st));
-  ksk_kernel<<<big * p.ks_level, 128, 0, st>>>(K->ksk, K->glwe_sk, K->lwe_sk, p.n, p.ks_level,
-                                               p.ks_base_log, K->seed, p.lwe_std * 0x1p64);
+  ksk_kernel<<<big * p.ks_level, 128, 0, st>>>(K->ksk, K->glwe_sk, K->lwe_sk, p.n, K->ksk_row,
+                                               p.ks_level, p.ks_base_log, K->seed,
+                                               p.lwe_std * 0x1p64);
   PNB_CHECK_LAUNCH("ksk_kernel");
   return PNB_OK;
 }

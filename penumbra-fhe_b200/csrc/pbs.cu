@@ -128,184 +128,155 @@ int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaSt
 }
 
 // ------------------------------------------------------------------------------------------
-// Keyswitch: out[c][t] = (t == n ? b_c : 0) - sum_{i,j} digit_{c,i,j} * KSK[i][j][t].
-// Block = 128 threads covering 256 output columns for KS_CT ciphertexts.
+// Keyswitch (tensor cores, ks_tc.cu): digit scratch from `digits` or the stream allocator.
 // ------------------------------------------------------------------------------------------
-constexpr int KS_CT = 32;    // ciphertexts per block
-constexpr int KS_ICH = 16;   // input coefficients staged per round
-constexpr int KS_MAXL = 8;   // maximum keyswitch levels
-
-__global__ void __launch_bounds__(128) keyswitch_kernel(const uint64_t* __restrict__ in,
-                                                        uint64_t* __restrict__ out,
-                                                        const uint64_t* __restrict__ ksk,
-                                                        int count, int n, int big, int base_log,
-                                                        int level) {
-  __shared__ int8_t dig[KS_CT][KS_ICH * KS_MAXL];
-  const int tid = threadIdx.x;
-  const int t0 = blockIdx.x * 256 + tid, t1 = t0 + 128;
-  const int c0 = blockIdx.y * KS_CT;
-  const int nct = min(KS_CT, count - c0);
-  const int row = n + 1;
-  uint64_t acc0[KS_CT], acc1[KS_CT];
-#pragma unroll
-  for (int c = 0; c < KS_CT; ++c) { acc0[c] = 0; acc1[c] = 0; }
-  const bool ok0 = t0 < row, ok1 = t1 < row;
-  const int total = base_log * level;
-  const uint64_t mask = (1ull << base_log) - 1, half = 1ull << (base_log - 1);
-
-  for (int i0 = 0; i0 < big; i0 += KS_ICH) {
-    __syncthreads();
-    for (int e = tid; e < KS_CT * KS_ICH; e += 128) {
-      const int c = e / KS_ICH, ii = e % KS_ICH;
-      if (c < nct && i0 + ii < big) {
-        uint64_t a = in[(size_t)(c0 + c) * (big + 1) + i0 + ii];
-        uint64_t st = (a >> (64 - total)) + ((a >> (63 - total)) & 1u);
-        for (int j = level - 1; j >= 0; --j) {
-          uint64_t d = st & mask;
-          st >>= base_log;
-          bool neg = d >= half;
-          dig[c][ii * KS_MAXL + j] = (int8_t)(neg ? (int64_t)d - (int64_t)(1ull << base_log)
-                                                  : (int64_t)d);
-          st += neg ? 1u : 0u;
-        }
-      } else {
-        for (int j = 0; j < level; ++j) dig[c][ii * KS_MAXL + j] = 0;
-      }
-    }
-    __syncthreads();
-    const int iimax = min(KS_ICH, big - i0);
-    for (int ii = 0; ii < iimax; ++ii) {
-      for (int j = 0; j < level; ++j) {
-        const uint64_t* kr = ksk + ((size_t)(i0 + ii) * level + j) * row;
-        const uint64_t k0 = ok0 ? __ldg(kr + t0) : 0, k1 = ok1 ? __ldg(kr + t1) : 0;
-#pragma unroll
-        for (int c = 0; c < KS_CT; ++c) {
-          const uint64_t d = (uint64_t)(int64_t)dig[c][ii * KS_MAXL + j];
-          acc0[c] -= d * k0;
-          acc1[c] -= d * k1;
-        }
-      }
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < KS_CT; ++c) {
-    if (c < nct) {
-      const uint64_t b = in[(size_t)(c0 + c) * (big + 1) + big];
-      if (ok0) out[(size_t)(c0 + c) * row + t0] = acc0[c] + (t0 == n ? b : 0);
-      if (ok1) out[(size_t)(c0 + c) * row + t1] = acc1[c] + (t1 == n ? b : 0);
-    }
-  }
-}
-
 int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,
-                     cudaStream_t st) {
-  const pnb_params& p = K->p;
-  // digits are staged as int8: |digit| <= 2^(base_log-1) must fit
-  if (p.ks_level > KS_MAXL || p.ks_base_log * p.ks_level >= 64 || p.ks_base_log < 1 ||
-      p.ks_base_log > 7) {
-    set_error("keyswitch: unsupported ks_base_log=%d ks_level=%d", p.ks_base_log, p.ks_level);
-    return PNB_ERR_UNSUPPORTED;
-  }
+                     void* digits, cudaStream_t st) {
   if (count <= 0) return PNB_OK;
-  dim3 grid((p.n + 1 + 255) / 256, (count + KS_CT - 1) / KS_CT);
-  keyswitch_kernel<<<grid, 128, 0, st>>>(in, out, K->ksk, count, p.n, p.k * p.N, p.ks_base_log,
-                                         p.ks_level);
-  PNB_CHECK_LAUNCH("keyswitch_kernel");
-  return PNB_OK;
+  void* d = digits;
+  bool own = false;
+  if (!d) {
+    cudaError_t e = cudaMallocAsync(&d, ks_tc_workspace_bytes(K->p, count), st);
+    if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync(keyswitch digits)");
+    own = true;
+  }
+  int rc = keyswitch_tc(K, in, out, count, d, st);
+  if (own) {
+    cudaError_t e = cudaFreeAsync(d, st);
+    if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(keyswitch digits)");
+  }
+  return rc;
 }
 
 // ------------------------------------------------------------------------------------------
 // Blind rotation + sample extraction, k = 1, pbs_level = 1, N = 2048.
-// One block of 2 warps per ciphertext; warp p owns GLWE polynomial p (0 = mask, 1 = body).
+//
+// A block bootstraps CPB ciphertexts in lockstep; warp (2c + p) owns GLWE polynomial p
+// (0 = mask, 1 = body) of ciphertext c.  The accumulator lives in shared memory as the top 32
+// bits of each torus coefficient: the f64 FFT product already carries ~2^37 of rounding error
+// per coefficient, so the dropped low word (<= 2^32, a random walk of ~2^35 after n updates)
+// sits far below both that and the bootstrap's own output noise (~2^49).  Warps of the same
+// output polynomial read the same bootstrapping-key lines right after a block barrier, so the
+// second and later ciphertexts of a block find them in L1.
 // ------------------------------------------------------------------------------------------
 constexpr int BR_MAXN = 1024;  // maximum small LWE dimension supported by the smem layout
 
-struct BrSmem {
-  uint64_t acc[2][FFT_N];
-  double2 buf[2][FFT_M];
-  uint16_t abar[BR_MAXN];
+template <int CPB>
+struct BrLayout {
+  static constexpr int WARPS = 2 * CPB;
+  static constexpr int SCRATCH = FFT_M * sizeof(double2);           // 16 KB per warp
+  static constexpr int ACC = FFT_N * sizeof(uint32_t);              // 8 KB per warp
+  static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);           // 2 KB per ciphertext
+  static constexpr int BYTES = WARPS * (SCRATCH + ACC) + CPB * ABAR;
 };
 
-__global__ void __launch_bounds__(64) blind_rotate_k1l1_kernel(
+__device__ __forceinline__ uint32_t rot_coef32(const uint32_t* P, int t, int r) {
+  int s = t - r;
+  bool neg = false;
+  if (s < 0) { s += FFT_N; neg = true; }
+  if (s < 0) { s += FFT_N; neg = false; }
+  const uint32_t v = P[s];
+  return neg ? 0u - v : v;
+}
+
+// Top 32 bits (rounded) of the integer nearest to v, modulo 2^64.
+__device__ __forceinline__ uint32_t f64_to_top32(double v) {
+  return (uint32_t)((f64_to_torus(v) + 0x80000000ull) >> 32);
+}
+
+template <int CPB>
+__global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
     const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
-    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int n, int base_log,
-    FftTables tb) {
+    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
+    int base_log, FftTables tb) {
+  using L = BrLayout<CPB>;
   extern __shared__ __align__(16) unsigned char br_raw[];
-  BrSmem& S = *reinterpret_cast<BrSmem*>(br_raw);
+  double2* scratch = reinterpret_cast<double2*>(br_raw);
+  uint32_t* accs = reinterpret_cast<uint32_t*>(br_raw + L::WARPS * L::SCRATCH);
+  uint16_t* abars = reinterpret_cast<uint16_t*>(br_raw + L::WARPS * (L::SCRATCH + L::ACC));
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int ct = blockIdx.x;
-  const uint64_t* in = small_ct + (size_t)ct * (n + 1);
+  const int cl = warp >> 1, p = warp & 1;
+  const int ct = blockIdx.x * CPB + cl;
+  const bool valid = ct < count;
   constexpr int LG = 12;  // log2(2N)
-  for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
-  const int bt = modswitch(in[n], LG);
+  uint16_t* abar = abars + cl * BR_MAXN;
+  uint32_t* acc = accs + warp * FFT_N;
+  double2* buf = scratch + warp * FFT_M;
+  const double2* obuf = scratch + (warp ^ 1) * FFT_M;
+
+  const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
+  const int t64 = threadIdx.x & 63;
+  for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
+  const int bt = valid ? modswitch(in[n], LG) : 0;
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = threadIdx.x; t < FFT_N; t += 64) {
-    S.acc[0][t] = 0;
-    S.acc[1][t] = rot_coef(tv, t, r0);
-  }
+  for (int t = lane; t < FFT_N; t += 32)
+    acc[t] = (p == 0) ? 0u : (uint32_t)((rot_coef(tv, t, r0) + 0x80000000ull) >> 32);
   __syncthreads();
 
-  uint64_t* my = S.acc[warp];
-  double2* mybuf = S.buf[warp];
-  const double2* otherbuf = S.buf[warp ^ 1];
-  const uint64_t rnd = 1ull << (63 - base_log);
-  const uint64_t dmask = (1ull << base_log) - 1, dhalf = 1ull << (base_log - 1);
+  const int shift = 32 - base_log;
+  const uint32_t rnd = 1u << (shift - 1);
+  const uint32_t dmask = (1u << base_log) - 1, dhalf = 1u << (base_log - 1);
 
   for (int i = 0; i < n; ++i) {
-    const int a = S.abar[i];
-    if (a == 0) continue;
+    const int a = abar[i];
     double2 x[FFT_R];
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
-      // Keep the shared-memory loads of a few coefficients in flight at a time: hoisting all
-      // 64 of them ahead of the conversions would exceed the register budget.
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      const uint64_t v0 = rot_coef(my, j, a) - my[j];
-      const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
-      // single-level signed digit: round to base_log bits, centre in [-B/2, B/2)
-      uint64_t s0 = ((v0 + rnd) >> (64 - base_log)) & dmask;
-      uint64_t s1 = ((v1 + rnd) >> (64 - base_log)) & dmask;
-      const int64_t d0 = s0 >= dhalf ? (int64_t)s0 - (int64_t)(dmask + 1) : (int64_t)s0;
-      const int64_t d1 = s1 >= dhalf ? (int64_t)s1 - (int64_t)(dmask + 1) : (int64_t)s1;
+      const uint32_t v0 = rot_coef32(acc, j, a) - acc[j];
+      const uint32_t v1 = rot_coef32(acc, j + FFT_M, a) - acc[j + FFT_M];
+      // single-level signed digit of the torus value whose top 32 bits are v
+      const uint32_t s0 = ((v0 + rnd) >> shift) & dmask;
+      const uint32_t s1 = ((v1 + rnd) >> shift) & dmask;
+      const int d0 = s0 >= dhalf ? (int)s0 - (int)(dmask + 1) : (int)s0;
+      const int d1 = s1 >= dhalf ? (int)s1 - (int)(dmask + 1) : (int)s1;
       x[m] = make_double2(small_int_to_f64(d0), small_int_to_f64(d1));
     }
-    fft_forward(x, mybuf, lane, tb);
+    fft_forward(x, buf, lane, tb);
 #pragma unroll
-    for (int r = 0; r < 32; ++r) mybuf[r * 32 + lane] = x[r];
+    for (int r = 0; r < 32; ++r) buf[r * 32 + lane] = x[r];
     __syncthreads();
-    // Output polynomial c = warp: D_own * F[own row][c] + D_other * F[other row][c].
+    // Output polynomial p of this ciphertext: D_own * F[own row][p] + D_other * F[other][p].
     const double2* g = fbsk + (size_t)i * 4 * FFT_M;
-    const double2* f_own = g + (size_t)(warp * 2 + warp) * FFT_M;
-    const double2* f_oth = g + (size_t)((warp ^ 1) * 2 + warp) * FFT_M;
+    const double2* f_own = g + (size_t)(p * 2 + p) * FFT_M;
+    const double2* f_oth = g + (size_t)((p ^ 1) * 2 + p) * FFT_M;
 #pragma unroll
     for (int r = 0; r < 32; ++r) {
-      if ((r & 3) == 0) asm volatile("" ::: "memory");
+      if ((r & 7) == 0) asm volatile("" ::: "memory");
       const int e = r * 32 + lane;
       const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
-      const double2 dt = otherbuf[e];
+      const double2 dt = obuf[e];
       const double2 p0 = cmul(x[r], fo);
       x[r] = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
                           p0.y + fma(dt.x, ft.y, dt.y * ft.x));
     }
     __syncthreads();
-    fft_inverse(x, mybuf, lane, tb);
+    fft_inverse(x, buf, lane, tb);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      my[j] += f64_to_torus(x[m].x);
-      my[j + FFT_M] += f64_to_torus(x[m].y);
+      acc[j] += f64_to_top32(x[m].x);
+      acc[j + FFT_M] += f64_to_top32(x[m].y);
     }
     __syncwarp();
   }
-  __syncthreads();
   // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
-  uint64_t* o = out + (size_t)ct * (FFT_N + 1);
-  for (int t = threadIdx.x; t < FFT_N; t += 64)
-    o[t] = (t == 0) ? S.acc[0][0] : (uint64_t)0 - S.acc[0][FFT_N - t];
-  if (threadIdx.x == 0) o[FFT_N] = S.acc[1][0];
+  if (valid) {
+    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    if (p == 0) {
+      for (int t = lane; t < FFT_N; t += 32) {
+        const uint64_t v = (uint64_t)acc[t == 0 ? 0 : FFT_N - t] << 32;
+        o[t] = (t == 0) ? v : (uint64_t)0 - v;
+      }
+    } else if (lane == 0) {
+      o[FFT_N] = (uint64_t)acc[0] << 32;
+    }
+  }
 }
+
+constexpr int BR_CPB = 2;
 
 static bool br_supported(const pnb_params& p) {
   return p.k == 1 && p.N == FFT_N && p.pbs_level == 1 && p.n <= BR_MAXN && p.n > 0 &&
@@ -323,18 +294,22 @@ int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* s
   FftTables tb;
   int rc = fft_tables_get(&tb);
   if (rc) return rc;
-  const int smem = sizeof(BrSmem);
-  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_k1l1_kernel,
+  constexpr int smem = BrLayout<BR_CPB>::BYTES;
+  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_kernel<BR_CPB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blind_rotate_k1l1_kernel<<<count, 64, smem, st>>>(small, tv, K->fbsk, out, K->p.n,
-                                                    K->p.pbs_base_log, tb);
-  PNB_CHECK_LAUNCH("blind_rotate_k1l1_kernel");
+  const int blocks = (count + BR_CPB - 1) / BR_CPB;
+  blind_rotate_kernel<BR_CPB><<<blocks, 64 * BR_CPB, smem, st>>>(
+      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+  PNB_CHECK_LAUNCH("blind_rotate_kernel");
   return PNB_OK;
 }
 
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
 size_t pbs_workspace_bytes(const pnb_keys* K, int count) {
   if (!K || count <= 0) return 0;
-  return (size_t)count * (K->p.n + 1) * sizeof(uint64_t);
+  return align256((size_t)count * (K->p.n + 1) * sizeof(uint64_t)) +
+         ks_tc_workspace_bytes(K->p, count);
 }
 
 int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
@@ -347,7 +322,7 @@ int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_
   if (count == 0) return PNB_OK;
   int rc = PNB_OK;
   const size_t need = pbs_workspace_bytes(K, count);
-  uint64_t* small = nullptr;
+  unsigned char* w = nullptr;
   bool own = false;
   if (ws) {
     if (ws_bytes < need) {
@@ -355,16 +330,22 @@ int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_
                 need);
       return PNB_ERR_INVALID;
     }
-    small = static_cast<uint64_t*>(ws);
+    if ((uintptr_t)ws % 256 != 0) {
+      set_error("pbs: workspace must be 256-byte aligned");
+      return PNB_ERR_INVALID;
+    }
+    w = static_cast<unsigned char*>(ws);
   } else {
-    cudaError_t e = cudaMallocAsync((void**)&small, need, st);
+    cudaError_t e = cudaMallocAsync((void**)&w, need, st);
     if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync(pbs workspace)");
     own = true;
   }
-  rc = keyswitch_launch(K, in, small, count, st);
+  uint64_t* small = reinterpret_cast<uint64_t*>(w);
+  void* digits = w + align256((size_t)count * (K->p.n + 1) * sizeof(uint64_t));
+  rc = keyswitch_launch(K, in, small, count, digits, st);
   if (rc == PNB_OK) rc = blind_rotate_launch(K, tv, small, out, count, st);
   if (own) {
-    cudaError_t e = cudaFreeAsync(small, st);
+    cudaError_t e = cudaFreeAsync(w, st);
     if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(pbs workspace)");
   }
   return rc;

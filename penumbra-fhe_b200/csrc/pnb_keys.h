@@ -14,7 +14,8 @@ struct pnb_keys {
   uint64_t* glwe_sk;   // [k*N]          GLWE secret key = big LWE key (client side)
   uint64_t* bsk;       // [n][(k+1)l][k+1][N] standard-domain bootstrapping key
   double2* fbsk;       // [n][(k+1)l][k+1][N/2] Fourier bootstrapping key (permuted spectrum)
-  uint64_t* ksk;       // [k*N][ks_level][n+1] keyswitching key
+  uint64_t* ksk;       // [k*N][ks_level][ksk_row] keyswitching key, rows padded to 16 bytes
+  int ksk_row;         // words per keyswitching-key row (n+1 rounded up to even)
   size_t bsk_words;
   size_t fbsk_elems;
   size_t ksk_words;
@@ -24,7 +25,7 @@ namespace pnb {
 int keygen_device(pnb_keys* K, cudaStream_t st);
 int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaStream_t st);
 int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,
-                     cudaStream_t st);
+                     void* digits, cudaStream_t st);
 int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
                         uint64_t* out, int count, cudaStream_t st);
 size_t pbs_workspace_bytes(const pnb_keys* K, int count);
@@ -41,4 +42,8 @@ int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count,
 int lwe_contract(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                  const uint64_t* X, uint64_t* Y, int batch, int lwe_len, cudaStream_t st);
 int measure_fp64_peak(double* tflops);
+int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count, void* digits,
+                 cudaStream_t st);
+size_t ks_tc_workspace_bytes(const pnb_params& p, int count);
+int tc_status_read_and_clear(int* out);
 }  // namespace pnb

@@ -55,7 +55,7 @@ def test_encrypt_bit_exact_and_decrypts(pnb, gkeys, okeys):
     assert torch.equal(pnb.decrypt_vec(gkeys, ct).cpu(), torch.tensor(msgs))
 
 
-@pytest.mark.parametrize("count", [1, 33, 70])
+@pytest.mark.parametrize("count", [1, 33, 130, 300])
 def test_keyswitch_bit_exact(pnb, gkeys, okeys, count):
     rng = np.random.default_rng(count)
     msgs = rng.integers(0, 16, count)
@@ -64,6 +64,7 @@ def test_keyswitch_bit_exact(pnb, gkeys, okeys, count):
     assert np.array_equal(_u64(ks), okeys.keyswitch(_u64(ct)))
     dec = okeys.decode(okeys.phase_small(_u64(ks)))
     assert np.array_equal(dec, msgs)
+    assert pnb.device_status(0) == 0
 
 
 def test_fft_negacyclic_product_precision(pnb, oracle):
@@ -113,6 +114,7 @@ def test_pbs_random_lut_batch_4096(pnb, gkeys, okeys):
     out = pnb.pbs_batch(gkeys, tv, ct)
     dec = pnb.decrypt_vec(gkeys, out).cpu().numpy()
     assert np.array_equal(dec, lut[msgs])
+    assert pnb.device_status(0) == 0
     # Noise level against the oracle's FFT bootstrap on the same keys and inputs.
     gpu_noise = _noise(_u64(pnb.phase(gkeys, out)), lut[msgs], gkeys.params.delta())
     sub = 256
