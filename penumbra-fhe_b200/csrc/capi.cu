@@ -307,7 +307,13 @@ int pnb_device_status(int device, int* status_out) {
   if (!status_out) { set_error("status_out is NULL"); return PNB_ERR_INVALID; }
   DeviceGuard g(device);
   if (g.rc) return g.rc;
-  return tc_status_read_and_clear(status_out);
+  int a = 0, b = 0;
+  int rc = tc_status_read_and_clear(&a);
+  if (rc) return rc;
+  rc = br_status_read_and_clear(&b);
+  if (rc) return rc;
+  *status_out = a ? a : (b ? 16 + b : 0);
+  return PNB_OK;
 }
 
 int pnb_measure_fp64_peak(int device, double* tflops_out) {

@@ -137,6 +137,46 @@ __device__ __forceinline__ void warp_transpose(double2 (&x)[FFT_R], double2* buf
   __syncwarp();
 }
 
+// The same transpose through an 8 KB buffer of 1024 doubles: real parts, then imaginary parts.
+__device__ __forceinline__ void warp_transpose_half(double2 (&x)[FFT_R], double* buf, int lane) {
+#pragma unroll
+  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r].x;
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 32; ++q) x[q].x = buf[lane * 32 + ((q + lane) & 31)];
+  __syncwarp();
+#pragma unroll
+  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r].y;
+  __syncwarp();
+#pragma unroll
+  for (int q = 0; q < 32; ++q) x[q].y = buf[lane * 32 + ((q + lane) & 31)];
+  __syncwarp();
+}
+
+// Forward / inverse FFT through the 8 KB half buffer; the twiddle tables are read through `tb`
+// as ordinary cached loads.
+__device__ __forceinline__ void fft_forward_h(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const FftTables& tb) {
+#pragma unroll
+  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], __ldg(&tb.twf[m]));
+  dft32_dif(x);
+#pragma unroll
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], __ldg(&tb.wf[r * 32 + lane]));
+  warp_transpose_half(x, buf, lane);
+  dft32_dif(x);
+}
+
+__device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const FftTables& tb) {
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.wi[n * 32 + lane]));
+  warp_transpose_half(x, buf, lane);
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.twi[n]));
+}
+
 // Forward negacyclic FFT of one folded polynomial (see header comment).
 __device__ __forceinline__ void fft_forward(double2 (&x)[FFT_R], double2* buf, int lane,
                                             const FftTables& tb) {

@@ -17,8 +17,21 @@
 #include "fft1024.cuh"
 #include "pnb_internal.cuh"
 #include "pnb_keys.h"
+#include "tc_primitives.cuh"
 
 namespace pnb {
+
+// Device-side status word of the blind rotation: non-zero when its bounded wait ran out.
+__device__ int g_br_status;
+
+int br_status_read_and_clear(int* out) {
+  int v = 0;
+  PNB_CUDA(cudaMemcpyFromSymbol(&v, g_br_status, sizeof(int)));
+  const int zero = 0;
+  PNB_CUDA(cudaMemcpyToSymbol(g_br_status, &zero, sizeof(int)));
+  *out = v;
+  return PNB_OK;
+}
 
 // ------------------------------------------------------------------------------------------
 // FFT tables (one set per device, built on first use).
@@ -164,10 +177,16 @@ constexpr int BR_MAXN = 1024;  // maximum small LWE dimension supported by the s
 template <int CPB>
 struct BrLayout {
   static constexpr int WARPS = 2 * CPB;
-  static constexpr int SCRATCH = FFT_M * sizeof(double2);           // 16 KB per warp
+  static constexpr int SCRATCH = FFT_M * sizeof(double);            // 8 KB per warp
   static constexpr int ACC = FFT_N * sizeof(uint32_t);              // 8 KB per warp
+  static constexpr int BSK = 4 * FFT_M * sizeof(double2);           // 64 KB: one GGSW (k=1,l=1)
   static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);           // 2 KB per ciphertext
-  static constexpr int BYTES = WARPS * (SCRATCH + ACC) + CPB * ABAR;
+  static constexpr int OFF_ACC = WARPS * SCRATCH;
+  static constexpr int OFF_BSK = OFF_ACC + WARPS * ACC;
+  static constexpr int OFF_ABAR = OFF_BSK + BSK;
+  static constexpr int OFF_BAR = OFF_ABAR + CPB * ABAR;
+  static constexpr int OFF_TAB = OFF_BAR + 16;
+  static constexpr int BYTES = OFF_TAB + (int)sizeof(FftTables);
 };
 
 __device__ __forceinline__ uint32_t rot_coef32(const uint32_t* P, int t, int r) {
@@ -184,25 +203,60 @@ __device__ __forceinline__ uint32_t f64_to_top32(double v) {
   return (uint32_t)((f64_to_torus(v) + 0x80000000ull) >> 32);
 }
 
+// Named barrier over the two warps of one ciphertext.
+__device__ __forceinline__ void pair_sync(int pair) {
+  asm volatile("bar.sync %0, 64;" ::"r"(pair + 1) : "memory");
+}
+
+constexpr uint32_t BR_WAIT_LIMIT = 1u << 24;
+
+// Stage GGSW number i of the Fourier bootstrapping key (64 KB) into shared memory.
+__device__ __forceinline__ void br_stage_ggsw(uint32_t dst, const double2* src, uint32_t bar) {
+  tc::mbar_expect_tx(bar, 4 * FFT_M * sizeof(double2));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst + q * FFT_M * 16u), "l"(src + q * FFT_M), "r"(FFT_M * 16u), "r"(bar)
+        : "memory");
+  }
+}
+
 template <int CPB>
-__global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
+__global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
-    int base_log, FftTables tb) {
+    int base_log, FftTables tb_param) {
   using L = BrLayout<CPB>;
-  extern __shared__ __align__(16) unsigned char br_raw[];
-  double2* scratch = reinterpret_cast<double2*>(br_raw);
-  uint32_t* accs = reinterpret_cast<uint32_t*>(br_raw + L::WARPS * L::SCRATCH);
-  uint16_t* abars = reinterpret_cast<uint16_t*>(br_raw + L::WARPS * (L::SCRATCH + L::ACC));
+  extern __shared__ __align__(128) unsigned char br_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cl = warp >> 1, p = warp & 1;
   const int ct = blockIdx.x * CPB + cl;
   const bool valid = ct < count;
   constexpr int LG = 12;  // log2(2N)
-  uint16_t* abar = abars + cl * BR_MAXN;
-  uint32_t* acc = accs + warp * FFT_N;
-  double2* buf = scratch + warp * FFT_M;
-  const double2* obuf = scratch + (warp ^ 1) * FFT_M;
+  double* buf = reinterpret_cast<double*>(br_raw) + warp * FFT_M;
+  double2* xbuf = reinterpret_cast<double2*>(buf);  // the same 8 KB seen as 512 complex
+  const double2* obuf = reinterpret_cast<const double2*>(reinterpret_cast<double*>(br_raw) +
+                                                         (warp ^ 1) * FFT_M);
+  uint32_t* acc = reinterpret_cast<uint32_t*>(br_raw + L::OFF_ACC) + warp * FFT_N;
+  const double2* bsk_s = reinterpret_cast<const double2*>(br_raw + L::OFF_BSK);
+  uint16_t* abar = reinterpret_cast<uint16_t*>(br_raw + L::OFF_ABAR) + cl * BR_MAXN;
+  const uint32_t bar = tc::smem_u32(br_raw + L::OFF_BAR);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(br_raw + L::OFF_BAR + 8);
+  const uint32_t bsk_dst = tc::smem_u32(br_raw + L::OFF_BSK);
+  volatile FftTables* tab_s = reinterpret_cast<volatile FftTables*>(br_raw + L::OFF_TAB);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+    *abort_s = 0;
+    tab_s->wf = tb_param.wf;
+    tab_s->wi = tb_param.wi;
+    tab_s->twf = tb_param.twf;
+    tab_s->twi = tb_param.twi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) br_stage_ggsw(bsk_dst, fbsk, bar);
 
   const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
   const int t64 = threadIdx.x & 63;
@@ -216,8 +270,16 @@ __global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
   const int shift = 32 - base_log;
   const uint32_t rnd = 1u << (shift - 1);
   const uint32_t dmask = (1u << base_log) - 1, dhalf = 1u << (base_log - 1);
+  const double2* f_own = bsk_s + (size_t)(p * 2 + p) * FFT_M;
+  const double2* f_oth = bsk_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
 
   for (int i = 0; i < n; ++i) {
+    // Twiddle pointers re-read every iteration so their loads are not hoisted out of the loop.
+    FftTables tb;
+    tb.wf = tab_s->wf;
+    tb.wi = tab_s->wi;
+    tb.twf = tab_s->twf;
+    tb.twi = tab_s->twi;
     const int a = abar[i];
     double2 x[FFT_R];
 #pragma unroll
@@ -233,26 +295,39 @@ __global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
       const int d1 = s1 >= dhalf ? (int)s1 - (int)(dmask + 1) : (int)s1;
       x[m] = make_double2(small_int_to_f64(d0), small_int_to_f64(d1));
     }
-    fft_forward(x, buf, lane, tb);
-#pragma unroll
-    for (int r = 0; r < 32; ++r) buf[r * 32 + lane] = x[r];
-    __syncthreads();
-    // Output polynomial p of this ciphertext: D_own * F[own row][p] + D_other * F[other][p].
-    const double2* g = fbsk + (size_t)i * 4 * FFT_M;
-    const double2* f_own = g + (size_t)(p * 2 + p) * FFT_M;
-    const double2* f_oth = g + (size_t)((p ^ 1) * 2 + p) * FFT_M;
-#pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      if ((r & 7) == 0) asm volatile("" ::: "memory");
-      const int e = r * 32 + lane;
-      const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
-      const double2 dt = obuf[e];
-      const double2 p0 = cmul(x[r], fo);
-      x[r] = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
-                          p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+    fft_forward_h(x, buf, lane, tb);
+    // GGSW i must have landed in shared memory (bounded wait; parity = i mod 2).
+    if (!tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT)) {
+      *abort_s = 1;
+      atomicExch(&g_br_status, 1);
     }
+    // Pointwise product in two halves of 16 registers, exchanged between the ciphertext's two
+    // warps: output polynomial p = D_own * F[own row][p] + D_other * F[other row][p].
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+#pragma unroll
+      for (int rr = 0; rr < 16; ++rr) xbuf[rr * 32 + lane] = x[16 * h + rr];
+      pair_sync(cl);
+#pragma unroll
+      for (int rr = 0; rr < 16; ++rr) {
+        const int r = 16 * h + rr;
+        const int e = r * 32 + lane;
+        const double2 fo = f_own[e], ft = f_oth[e];
+        const double2 dt = obuf[rr * 32 + lane];
+        const double2 p0 = cmul(x[r], fo);
+        x[r] = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
+                            p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+      }
+      pair_sync(cl);
+    }
+    // Every warp is done with GGSW i: stage GGSW i+1 while the inverse FFTs run.
     __syncthreads();
-    fft_inverse(x, buf, lane, tb);
+    if (*abort_s) break;  // uniform: read by every thread after the same barrier
+    if (threadIdx.x == 0 && i + 1 < n) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
+    }
+    fft_inverse_h(x, buf, lane, tb);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
@@ -263,7 +338,7 @@ __global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
     __syncwarp();
   }
   // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
-  if (valid) {
+  if (valid && !*abort_s) {
     uint64_t* o = out + (size_t)ct * (FFT_N + 1);
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32) {
@@ -276,7 +351,7 @@ __global__ void __launch_bounds__(64 * CPB) blind_rotate_kernel(
   }
 }
 
-constexpr int BR_CPB = 2;
+constexpr int BR_CPB = 4;
 
 static bool br_supported(const pnb_params& p) {
   return p.k == 1 && p.N == FFT_N && p.pbs_level == 1 && p.n <= BR_MAXN && p.n > 0 &&
