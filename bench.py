@@ -254,7 +254,7 @@ def run_gpu(args):
                 "frac": achieved / peak,
                 "peak_source": "FP64 FMA probe measured in this run (no FP64 entry in "
                                "MEASURED_PEAKS.json)",
-                "kernel": "blind_rotate_k1l1_kernel",
+                "kernel": "blind_rotate_kernel<4>",
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
     cpu = None

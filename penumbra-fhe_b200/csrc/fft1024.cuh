@@ -153,28 +153,28 @@ __device__ __forceinline__ void warp_transpose_half(double2 (&x)[FFT_R], double*
   __syncwarp();
 }
 
-// Forward / inverse FFT through the 8 KB half buffer; the twiddle tables are read through `tb`
-// as ordinary cached loads.
+// Forward / inverse FFT through the 8 KB half buffer.  The forward twiddles come from shared
+// memory (`wf_s`, `twf_s`); the inverse ones from the cached global table and `twi_s`.
 __device__ __forceinline__ void fft_forward_h(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const FftTables& tb) {
+                                              const double2* wf_s, const double2* twf_s) {
 #pragma unroll
-  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], __ldg(&tb.twf[m]));
+  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], twf_s[m]);
   dft32_dif(x);
 #pragma unroll
-  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], __ldg(&tb.wf[r * 32 + lane]));
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], wf_s[r * 32 + lane]);
   warp_transpose_half(x, buf, lane);
   dft32_dif(x);
 }
 
 __device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const FftTables& tb) {
+                                              const double2* wi_g, const double2* twi_s) {
   idft32_dit(x);
 #pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.wi[n * 32 + lane]));
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&wi_g[n * 32 + lane]));
   warp_transpose_half(x, buf, lane);
   idft32_dit(x);
 #pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&tb.twi[n]));
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], twi_s[n]);
 }
 
 // Forward negacyclic FFT of one folded polynomial (see header comment).

@@ -183,24 +183,25 @@ struct BrLayout {
   static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);           // 2 KB per ciphertext
   static constexpr int OFF_ACC = WARPS * SCRATCH;
   static constexpr int OFF_BSK = OFF_ACC + WARPS * ACC;
-  static constexpr int OFF_ABAR = OFF_BSK + BSK;
+  static constexpr int OFF_WF = OFF_BSK + BSK;                      // 16 KB forward twiddles
+  static constexpr int OFF_TWF = OFF_WF + FFT_M * (int)sizeof(double2);
+  static constexpr int OFF_TWI = OFF_TWF + 32 * (int)sizeof(double2);
+  static constexpr int OFF_ABAR = OFF_TWI + 32 * (int)sizeof(double2);
   static constexpr int OFF_BAR = OFF_ABAR + CPB * ABAR;
   static constexpr int OFF_TAB = OFF_BAR + 16;
-  static constexpr int BYTES = OFF_TAB + (int)sizeof(FftTables);
+  static constexpr int BYTES = OFF_TAB + 16;
 };
 
-__device__ __forceinline__ uint32_t rot_coef32(const uint32_t* P, int t, int r) {
-  int s = t - r;
-  bool neg = false;
-  if (s < 0) { s += FFT_N; neg = true; }
-  if (s < 0) { s += FFT_N; neg = false; }
-  const uint32_t v = P[s];
-  return neg ? 0u - v : v;
-}
-
-// Top 32 bits (rounded) of the integer nearest to v, modulo 2^64.
-__device__ __forceinline__ uint32_t f64_to_top32(double v) {
-  return (uint32_t)((f64_to_torus(v) + 0x80000000ull) >> 32);
+// The blind rotation's inverse FFT leaves v * 2^-32, v the integer nearest the exact product
+// coefficient (|v| < 2^100).  Return round(v / 2^32) mod 2^32 -- the top word of the torus
+// value -- with four FP64 operations and no integer work: w = v 2^-32 reduced by the nearest
+// multiple of 2^32 is exact (|t| <= 2^31), and adding 1.5 * 2^52 rounds t into the low
+// mantissa word.
+__device__ __forceinline__ uint32_t scaled_f64_to_top32(double w) {
+  const double magic = 6755399441055744.0;  // 1.5 * 2^52
+  const double k = fma(w, 0x1p-32, magic) - magic;
+  const double t = fma(-4294967296.0, k, w);
+  return (uint32_t)__double2loint(t + magic);
 }
 
 // Named barrier over the two warps of one ciphertext.
@@ -226,7 +227,7 @@ template <int CPB>
 __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
-    int base_log, FftTables tb_param) {
+    int base_log, FftTables tb) {
   using L = BrLayout<CPB>;
   extern __shared__ __align__(128) unsigned char br_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -240,20 +241,26 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
                                                          (warp ^ 1) * FFT_M);
   uint32_t* acc = reinterpret_cast<uint32_t*>(br_raw + L::OFF_ACC) + warp * FFT_N;
   const double2* bsk_s = reinterpret_cast<const double2*>(br_raw + L::OFF_BSK);
+  double2* wf_s = reinterpret_cast<double2*>(br_raw + L::OFF_WF);
+  double2* twf_s = reinterpret_cast<double2*>(br_raw + L::OFF_TWF);
+  double2* twi_s = reinterpret_cast<double2*>(br_raw + L::OFF_TWI);
   uint16_t* abar = reinterpret_cast<uint16_t*>(br_raw + L::OFF_ABAR) + cl * BR_MAXN;
   const uint32_t bar = tc::smem_u32(br_raw + L::OFF_BAR);
   volatile int* abort_s = reinterpret_cast<volatile int*>(br_raw + L::OFF_BAR + 8);
   const uint32_t bsk_dst = tc::smem_u32(br_raw + L::OFF_BSK);
-  volatile FftTables* tab_s = reinterpret_cast<volatile FftTables*>(br_raw + L::OFF_TAB);
+  const double2* volatile* wi_s = reinterpret_cast<const double2* volatile*>(br_raw + L::OFF_TAB);
 
   if (threadIdx.x == 0) {
     tc::mbar_init(bar, 1);
     tc::fence_mbar_init();
     *abort_s = 0;
-    tab_s->wf = tb_param.wf;
-    tab_s->wi = tb_param.wi;
-    tab_s->twf = tb_param.twf;
-    tab_s->twi = tb_param.twi;
+    *wi_s = tb.wi;
+  }
+  for (int e = threadIdx.x; e < FFT_M; e += 64 * CPB) wf_s[e] = tb.wf[e];
+  if (threadIdx.x < 32) {
+    twf_s[threadIdx.x] = tb.twf[threadIdx.x];
+    const double2 t = tb.twi[threadIdx.x];
+    twi_s[threadIdx.x] = make_double2(t.x * 0x1p-32, t.y * 0x1p-32);  // exact scaling
   }
   __syncthreads();
   if (threadIdx.x == 0) br_stage_ggsw(bsk_dst, fbsk, bar);
@@ -269,33 +276,31 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 
   const int shift = 32 - base_log;
   const uint32_t rnd = 1u << (shift - 1);
-  const uint32_t dmask = (1u << base_log) - 1, dhalf = 1u << (base_log - 1);
   const double2* f_own = bsk_s + (size_t)(p * 2 + p) * FFT_M;
   const double2* f_oth = bsk_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
 
   for (int i = 0; i < n; ++i) {
-    // Twiddle pointers re-read every iteration so their loads are not hoisted out of the loop.
-    FftTables tb;
-    tb.wf = tab_s->wf;
-    tb.wi = tab_s->wi;
-    tb.twf = tab_s->twf;
-    tb.twi = tab_s->twi;
+    const double2* wi_g = *wi_s;  // re-read so the inverse-twiddle loads stay inside the loop
     const int a = abar[i];
+    // X^a = (-1)^(a >= N) X^(a mod N): rotate by ar in [0, N), flip the sign where it wraps.
+    const int ar = a & (FFT_N - 1);
+    const uint32_t flip0 = (a >= FFT_N) ? 0xffffffffu : 0u;
     double2 x[FFT_R];
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      const uint32_t v0 = rot_coef32(acc, j, a) - acc[j];
-      const uint32_t v1 = rot_coef32(acc, j + FFT_M, a) - acc[j + FFT_M];
-      // single-level signed digit of the torus value whose top 32 bits are v
-      const uint32_t s0 = ((v0 + rnd) >> shift) & dmask;
-      const uint32_t s1 = ((v1 + rnd) >> shift) & dmask;
-      const int d0 = s0 >= dhalf ? (int)s0 - (int)(dmask + 1) : (int)s0;
-      const int d1 = s1 >= dhalf ? (int)s1 - (int)(dmask + 1) : (int)s1;
-      x[m] = make_double2(small_int_to_f64(d0), small_int_to_f64(d1));
+      const int s0 = j - ar, s1 = j + FFT_M - ar;
+      const uint32_t w0 = (s0 < 0) ? ~flip0 : flip0, w1 = (s1 < 0) ? ~flip0 : flip0;
+      const uint32_t g0 = acc[s0 & (FFT_N - 1)], g1 = acc[s1 & (FFT_N - 1)];
+      const uint32_t v0 = ((g0 ^ w0) - w0) - acc[j];          // (+/- g0) - acc[j]
+      const uint32_t v1 = ((g1 ^ w1) - w1) - acc[j + FFT_M];
+      // Balanced digit of the top base_log bits: arithmetic shift of the rounded 32-bit word.
+      const int d0 = (int)(v0 + rnd) >> shift;
+      const int d1 = (int)(v1 + rnd) >> shift;
+      x[m] = make_double2((double)d0, (double)d1);
     }
-    fft_forward_h(x, buf, lane, tb);
+    fft_forward_h(x, buf, lane, wf_s, twf_s);
     // GGSW i must have landed in shared memory (bounded wait; parity = i mod 2).
     if (!tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT)) {
       *abort_s = 1;
@@ -327,13 +332,13 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
     }
-    fft_inverse_h(x, buf, lane, tb);
+    fft_inverse_h(x, buf, lane, wi_g, twi_s);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      acc[j] += f64_to_top32(x[m].x);
-      acc[j + FFT_M] += f64_to_top32(x[m].y);
+      acc[j] += scaled_f64_to_top32(x[m].x);
+      acc[j + FFT_M] += scaled_f64_to_top32(x[m].y);
     }
     __syncwarp();
   }
