@@ -118,6 +118,19 @@ int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* 
                   uint64_t* out_dev, int count, void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/* pnb_pbs_batch without any device allocation, for callers that cannot allocate GPU memory on
+ * this path (memory already reserved by another framework's caching allocator, request loops
+ * that must not pay allocator latency or synchronisation, FFI callers that keep a fixed device
+ * footprint after start-up).  The scratch is a fixed 4 MiB array that every GPU loading the
+ * library holds until exit; with the default parameter set a call takes at most 247
+ * ciphertexts and larger counts are rejected with PNB_ERR_INVALID (split the batch).  The
+ * first call on a device looks up that array's device address; make that first call before
+ * any stream capture.  Calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  The key set must come from pnb_keygen on the same device.
+ * No counterpart in the reference. */
+int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
+                          uint64_t* out_dev, int count, void* stream);
+
 /* Ciphertext x cleartext-weight contraction over LWE vectors mod 2^64:
  *   Y[b][j][c] = sum_i W[j][i] * X[b][i][c]  + (c == lwe_len-1 ? bias[j]*delta : 0)
  * W is int8 row-major [M][K], bias int64 [M] (may be NULL), X [batch][K][lwe_len],

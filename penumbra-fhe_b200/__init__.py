@@ -20,7 +20,7 @@ __all__ = [
     "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "fft_negacyclic_mul", "measure_fp64_peak",
-    "device_status",
+    "device_status", "pbs_batch_noalloc",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -76,6 +76,8 @@ _SIGS = {
     "pnb_pbs_workspace_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
     "pnb_pbs_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                 C.c_void_p, C.c_size_t, C.c_void_p]),
+    "pnb_pbs_batch_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                        C.c_void_p]),
     "pnb_lwe_contract": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -309,6 +311,22 @@ def pbs_batch(keys: KeySet, tv: torch.Tensor, ct: torch.Tensor,
     _check("pnb_pbs_batch",
            lib().pnb_pbs_batch(keys.handle, _ptr(tv), _ptr(ct), _ptr(out), count,
                                _ptr(workspace), ws_bytes, _stream(ct.device)))
+    return out
+
+
+def pbs_batch_noalloc(keys: KeySet, tv: torch.Tensor, ct: torch.Tensor,
+                      out: torch.Tensor) -> torch.Tensor:
+    """Bootstrap into a caller-provided ``out`` with no device allocation inside the library.
+
+    For callers that cannot allocate GPU memory on this path; the library's fixed 4 MiB
+    scratch limits a call to 247 ciphertexts with the default parameters, and concurrent calls
+    on the GPU race on that scratch.
+    """
+    ct = _u64(ct).contiguous()
+    count = ct.numel() // (keys.big_dim + 1)
+    _check("pnb_pbs_batch_noalloc",
+           lib().pnb_pbs_batch_noalloc(keys.handle, _ptr(tv), _ptr(ct), _ptr(out), count,
+                                       _stream(ct.device)))
     return out
 
 

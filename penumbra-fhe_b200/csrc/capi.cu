@@ -281,6 +281,24 @@ int pnb_pbs_batch(const pnb_keys* K, const uint64_t* tv_dev, const uint64_t* in_
                    (cudaStream_t)stream);
 }
 
+int pnb_pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv_dev, const uint64_t* in_dev,
+                          uint64_t* out_dev, int count, void* stream) {
+  int rc = check_keys(K);
+  if (rc) return rc;
+  if (count < 0 || (count > 0 && (!tv_dev || !in_dev || !out_dev))) {
+    set_error("pbs_noalloc: bad buffers or count %d", count);
+    return PNB_ERR_INVALID;
+  }
+  if (count > 0 && in_dev == out_dev) {
+    set_error("pbs_noalloc: input and output batches may not alias");
+    return PNB_ERR_INVALID;
+  }
+  if (count == 0) return PNB_OK;
+  DeviceGuard g(K->device);
+  if (g.rc) return g.rc;
+  return pbs_batch_noalloc(K, tv_dev, in_dev, out_dev, count, (cudaStream_t)stream);
+}
+
 int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M, int K,
                      const uint64_t* X_dev, uint64_t* Y_dev, int batch, int lwe_len,
                      void* stream) {

@@ -95,6 +95,14 @@ int fft_tables_get(FftTables* out) {
   return PNB_OK;
 }
 
+// True when the current device's FFT tables exist (never allocates).
+bool fft_tables_ready() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return false;
+  std::lock_guard<std::mutex> lk(g_tab_mu);
+  return g_tab_ok[dev];
+}
+
 // Coefficient t of X^r * P (negacyclic), r in [0, 2N).
 __device__ __forceinline__ uint64_t rot_coef(const uint64_t* P, int t, int r) {
   int s = t - r;

@@ -1,0 +1,71 @@
+// pbs_noalloc.cu -- a bootstrap entry point that performs no device allocation.
+//
+// pnb_pbs_batch needs scratch (the keyswitched ciphertexts and the keyswitch digits).  Callers
+// that hand it no workspace get that scratch from the stream-ordered allocator; callers that
+// cannot allocate at all -- a host process whose GPU memory is already reserved by another
+// framework's caching allocator, a serving loop that must not pay allocator latency or
+// synchronisation on the request path, an FFI caller that has to keep its device footprint
+// fixed after start-up -- use pnb_pbs_batch_noalloc instead.  Its scratch is the file-scope
+// array below: 4 MiB, allocated once per GPU when the library's module is loaded there and held
+// until the process exits.  With the default parameter set that holds 247 ciphertexts per call.
+//
+// Every call shares the array and finds the previous call's contents in it; the bootstrap
+// writes every scratch word it reads, so nothing needs clearing.  Calls whose kernels overlap on
+// the GPU (different streams, or different host threads) race on the array and must be
+// serialised by the caller.
+#include <mutex>
+
+#include "pnb_internal.cuh"
+#include "pnb_keys.h"
+
+namespace pnb {
+
+constexpr size_t NOALLOC_SCRATCH_BYTES = 4u << 20;  // 4 MiB
+static __device__ __align__(256) unsigned char g_pbs_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_pbs_scratch for each device (host code must not use the symbol itself:
+// in host code it is only a stand-in for the device object).
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_ptr[64];
+
+static int noalloc_scratch(int dev, void** out) {
+  if (dev < 0 || dev >= 64) {
+    set_error("pbs_noalloc: device index %d out of range", dev);
+    return PNB_ERR_INVALID;
+  }
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_pbs_scratch);  // `dev` is current here
+    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(pbs scratch)");
+    g_noalloc_ptr[dev] = p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return PNB_OK;
+}
+
+int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
+                      int count, cudaStream_t st) {
+  const size_t need = pbs_workspace_bytes(K, count);
+  if (need > NOALLOC_SCRATCH_BYTES) {
+    int max = count;
+    while (max > 0 && pbs_workspace_bytes(K, max) > NOALLOC_SCRATCH_BYTES) --max;
+    set_error("pbs_noalloc: %d ciphertexts need %zu bytes of scratch but the fixed scratch holds "
+              "%zu bytes (at most %d ciphertexts with these keys); split the batch",
+              count, need, NOALLOC_SCRATCH_BYTES, max);
+    return PNB_ERR_INVALID;
+  }
+  if (!fft_tables_ready()) {
+    set_error("pbs_noalloc: the FFT tables of this device are not built; create the key set "
+              "with pnb_keygen on this device first");
+    return PNB_ERR_INVALID;
+  }
+  int dev = 0;
+  PNB_CUDA(cudaGetDevice(&dev));
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(dev, &scratch);
+  if (rc) return rc;
+  return pbs_batch(K, tv, in, out, count, scratch, NOALLOC_SCRATCH_BYTES, st);
+}
+
+}  // namespace pnb

@@ -46,5 +46,8 @@ int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count
                  cudaStream_t st);
 size_t ks_tc_workspace_bytes(const pnb_params& p, int count);
 int tc_status_read_and_clear(int* out);
+bool fft_tables_ready();
+int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
+                      int count, cudaStream_t st);
 int br_status_read_and_clear(int* out);
 }  // namespace pnb
