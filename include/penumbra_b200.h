@@ -131,16 +131,25 @@ int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* 
 int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
                           uint64_t* out_dev, int count, void* stream);
 
-/* Ciphertext x cleartext-weight contraction over LWE vectors mod 2^64:
+/* Ciphertext x cleartext-weight contraction over LWE vectors mod 2^64, on the tensor cores:
  *   Y[b][j][c] = sum_i W[j][i] * X[b][i][c]  + (c == lwe_len-1 ? bias[j]*delta : 0)
- * W is int8 row-major [M][K], bias int64 [M] (may be NULL), X [batch][K][lwe_len],
- * Y [batch][M][lwe_len].
+ * W is int8 row-major [M][K] (K <= 65536), bias int64 [M] (may be NULL), X [batch][K][lwe_len],
+ * Y [batch][M][lwe_len].  Runs on the current device.
  * Replaces: the per-row scalar_mul_parallelized / add_parallelized / scalar_add_parallelized
- * loops of Linear::eval (runtime/src/ops/linear.rs:52-75) and Conv2d::eval after im2col
- * (runtime/src/ops/conv2d.rs:91-139). */
+ * loops of Linear::eval (runtime/src/ops/linear.rs:52-75). */
 int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M, int K,
                      const uint64_t* X_dev, uint64_t* Y_dev, int batch, int lwe_len,
                      void* stream);
+
+/* Gathered contraction: Y[g][j][c] = sum_k W[j][k] * X[index[g][k]][c] (+ bias on the body),
+ * index int32 [groups][K] selecting ciphertexts of X ([*][lwe_len]), -1 = a zero ciphertext.
+ * An implicit im2col: one group per (sample, output position) of a convolution, or per pooling
+ * window with W = 1.  Runs on the current device.
+ * Replaces: Conv2d::eval's tap loops (runtime/src/ops/conv2d.rs:91-139) and the avg window sums
+ * of Pool::eval (runtime/src/ops/pool.rs:110-118). */
+int pnb_lwe_contract_gather(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M,
+                            int K, const uint64_t* X_dev, const int32_t* index_dev, int groups,
+                            uint64_t* Y_dev, int lwe_len, void* stream);
 
 /* Negacyclic products out[c] = a[c] * b[c] mod (X^N + 1) through the same f64 FFT the blind
  * rotation uses (a: small signed integers, |a| < 2^31; b: u64 torus), count polynomials.
@@ -148,8 +157,9 @@ int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delt
 int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64_t* b_dev,
                            uint64_t* out_dev, int count, void* stream);
 
-/* Read and clear the device status word of the tensor-core kernels: 0 when no bounded wait ran
- * out since the last read, non-zero (the waiting role) otherwise.  No reference counterpart. */
+/* Read and clear the device status words of the kernels with bounded waits: 0 when no wait ran
+ * out since the last read; otherwise 1-3 keyswitch (producer, MMA, epilogue), 17 blind
+ * rotation, 33 contraction.  No reference counterpart. */
 int pnb_device_status(int device, int* status_out);
 
 /* Measure this device's FP64 FMA throughput (TFLOP/s) with a short register-only kernel; the

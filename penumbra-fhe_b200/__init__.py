@@ -19,7 +19,7 @@ __all__ = [
     "Params", "default_params", "KeySet", "keygen", "lib", "LibraryError",
     "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
     "pbs_batch", "blind_rotate",
-    "pbs_workspace_bytes", "lwe_contract", "fft_negacyclic_mul", "measure_fp64_peak",
+    "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
     "device_status", "pbs_batch_noalloc",
 ]
 
@@ -78,6 +78,9 @@ _SIGS = {
                                 C.c_void_p, C.c_size_t, C.c_void_p]),
     "pnb_pbs_batch_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                         C.c_void_p]),
+    "pnb_lwe_contract_gather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
+                                          C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                          C.c_void_p]),
     "pnb_lwe_contract": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
@@ -347,6 +350,30 @@ def lwe_contract(W: torch.Tensor, bias: torch.Tensor | None, delta: int, X: torc
                lib().pnb_lwe_contract(_ptr(W.contiguous()), _ptr(bias_t), delta % (1 << 64), M,
                                       K, _ptr(_u64(X).contiguous()), _ptr(out), B, L,
                                       _stream(X.device)))
+    return out
+
+
+def lwe_contract_gather(W: torch.Tensor, bias: torch.Tensor | None, delta: int,
+                        X: torch.Tensor, index: torch.Tensor,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """``Y[g, j, :] = sum_k W[j, k] X[index[g, k], :] + bias[j] * delta`` (index -1 = zero)."""
+    if W.dtype != torch.int8 or index.dtype != torch.int32:
+        raise TypeError("W must be int8 and index int32")
+    M, K = W.shape
+    G, K2 = index.shape
+    if K2 != K:
+        raise ValueError(f"index has {K2} taps, W expects {K}")
+    L = X.shape[-1]
+    if out is None:
+        out = torch.empty((G, M, L), dtype=torch.int64, device=X.device)
+    bias_t = None if bias is None else bias.to(device=X.device, dtype=torch.int64).contiguous()
+    with torch.cuda.device(X.device):
+        _check("pnb_lwe_contract_gather",
+               lib().pnb_lwe_contract_gather(_ptr(W.contiguous()), _ptr(bias_t),
+                                             delta % (1 << 64), M, K,
+                                             _ptr(_u64(X).contiguous()),
+                                             _ptr(index.contiguous()), G, _ptr(out), L,
+                                             _stream(X.device)))
     return out
 
 

@@ -306,8 +306,19 @@ int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delt
     set_error("contract: NULL buffer");
     return PNB_ERR_INVALID;
   }
-  return lwe_contract(W_dev, bias_dev, delta, M, K, X_dev, Y_dev, batch, lwe_len,
-                      (cudaStream_t)stream);
+  return lwe_contract_tc(W_dev, bias_dev, delta, M, K, X_dev, Y_dev, batch, lwe_len,
+                         (cudaStream_t)stream);
+}
+
+int pnb_lwe_contract_gather(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M,
+                            int K, const uint64_t* X_dev, const int32_t* index_dev, int groups,
+                            uint64_t* Y_dev, int lwe_len, void* stream) {
+  if (groups > 0 && (!W_dev || !X_dev || !index_dev || !Y_dev)) {
+    set_error("contract_gather: NULL buffer");
+    return PNB_ERR_INVALID;
+  }
+  return lwe_contract_gather(W_dev, bias_dev, delta, M, K, X_dev, index_dev, groups, Y_dev,
+                             lwe_len, (cudaStream_t)stream);
 }
 
 int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64_t* b_dev,
@@ -325,12 +336,14 @@ int pnb_device_status(int device, int* status_out) {
   if (!status_out) { set_error("status_out is NULL"); return PNB_ERR_INVALID; }
   DeviceGuard g(device);
   if (g.rc) return g.rc;
-  int a = 0, b = 0;
+  int a = 0, b = 0, c = 0;
   int rc = tc_status_read_and_clear(&a);
   if (rc) return rc;
   rc = br_status_read_and_clear(&b);
   if (rc) return rc;
-  *status_out = a ? a : (b ? 16 + b : 0);
+  rc = ct_status_read_and_clear(&c);
+  if (rc) return rc;
+  *status_out = a ? a : (b ? 16 + b : (c ? 32 + c : 0));
   return PNB_OK;
 }
 

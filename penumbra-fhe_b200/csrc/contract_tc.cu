@@ -1,0 +1,335 @@
+// contract_tc.cu -- ciphertext x cleartext-weight contraction on the tensor cores.
+//
+// Replaces the scalar_mul_parallelized / add_parallelized / scalar_add_parallelized loops of
+// Linear::eval (runtime/src/ops/linear.rs:52-75), Conv2d::eval (runtime/src/ops/conv2d.rs:91-139)
+// and the window sums of Pool::eval (runtime/src/ops/pool.rs:110-118).  All three are
+//     Y[g][j][c] = sum_k W[j][k] * X[idx[g][k]][c]   (+ bias[j] * delta on the body c = L-1)
+// over LWE ciphertexts of L words mod 2^64: a Linear layer is idx[g][k] = g*K + k, a
+// convolution is an implicit im2col (idx = input ciphertext under tap k of output position g,
+// -1 for zero padding), an average pool is W = 1 over the window.
+//
+// Each u64 word is 8 little-endian bytes, so for one group g the operand X[idx[g][:]][:] is a
+// u8 matrix [K][8L] that is N-contiguous: tcgen05.mma kind::i8 consumes it as an MN-major B
+// operand (A = W, s8, K-major) and the epilogue recombines the 8 byte-limb accumulators:
+//     Y = sum_b C[.][8c + b] << 8b   (mod 2^64),  |C| <= 128 * 255 * K < 2^31 for K < 65794.
+//
+// Ciphertext rows are L = kN+1 words (not a 16-byte multiple), so the B tiles are gathered
+// with 8-byte cp.async straight into the SWIZZLE_128B layout rather than by TMA; W (padded on
+// the device to [Mp][Kp]) comes by TMA.  Persistent CTAs walk (group, M tile, N tile) tiles;
+// 4 warps gather, 1 warp issues TMA + MMA, 4 warps run the epilogue from double-buffered TMEM
+// accumulators (2 x 256 columns).
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "pnb_internal.cuh"
+#include "pnb_keys.h"
+#include "tc_primitives.cuh"
+
+namespace pnb {
+
+// Status word of the contraction kernel: non-zero when one of its bounded waits ran out.
+__device__ int g_ct_status;
+
+int ct_status_read_and_clear(int* out) {
+  int v = 0;
+  PNB_CUDA(cudaMemcpyFromSymbol(&v, g_ct_status, sizeof(int)));
+  const int zero = 0;
+  PNB_CUDA(cudaMemcpyToSymbol(g_ct_status, &zero, sizeof(int)));
+  *out = v;
+  return PNB_OK;
+}
+
+int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                    uint64_t pitch_bytes, uint32_t box_inner, uint32_t box_outer);
+
+constexpr int CT_BM = 128;                   // output rows per tile
+constexpr int CT_BN = 256;                   // B bytes per tile = 32 output words
+constexpr int CT_BK = 128;                   // K per stage
+constexpr int CT_STAGES = 4;
+constexpr int CT_A_BYTES = CT_BM * CT_BK;    // 16 KB
+constexpr int CT_B_BYTES = CT_BK * CT_BN;    // 32 KB
+constexpr int CT_STAGE_BYTES = CT_A_BYTES + CT_B_BYTES;
+constexpr int CT_PRODUCERS = 128;            // gathering threads (warps 0..3)
+constexpr int CT_THREADS = 288;              // + MMA warp (4) + epilogue warps (5..8)
+constexpr int CT_SMEM = CT_STAGES * CT_STAGE_BYTES + 1024 + 256;
+constexpr uint32_t CT_IDESC = tc::idesc_i8(CT_BM, CT_BN, /*a_signed=*/true,
+                                           /*b_signed=*/false, /*a_mn=*/false, /*b_mn=*/true);
+constexpr uint32_t CT_WAIT_LIMIT = 1u << 24;
+
+struct CtArgs {
+  const uint64_t* X;       // ciphertexts [*][L]
+  const int32_t* idx;      // [G][K] ciphertext index into X, -1 = zero
+  const int64_t* bias;     // [M] or null
+  uint64_t* Y;             // [G][M][L]
+  uint64_t delta;
+  int G, M, K, L;
+  int m_tiles, n_tiles, k_blocks;
+};
+
+__device__ __forceinline__ void cp_async8(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+
+// Bounded wait that also gives up as soon as another role has flagged an abort.
+__device__ __forceinline__ bool ct_wait(uint32_t bar, uint32_t parity, volatile int* abort_s) {
+  for (uint32_t it = 0; it < CT_WAIT_LIMIT; it += 1024) {
+    if (tc::mbar_wait(bar, parity, 1024)) return true;
+    if (*abort_s) return false;
+  }
+  *abort_s = 1;
+  atomicExch(&g_ct_status, 1);
+  return false;
+}
+
+__global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
+    const __grid_constant__ CUtensorMap tmW, CtArgs a) {
+  extern __shared__ unsigned char ct_raw[];
+  const uint32_t raw = tc::smem_u32(ct_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  const uint32_t bars = base + CT_STAGES * CT_STAGE_BYTES;
+  auto full = [&](int s) { return bars + 8u * s; };
+  auto empty = [&](int s) { return bars + 8u * (CT_STAGES + s); };
+  auto acc_full = [&](int b) { return bars + 8u * (2 * CT_STAGES + b); };
+  auto acc_empty = [&](int b) { return bars + 8u * (2 * CT_STAGES + 2 + b); };
+  const uint32_t holder = bars + 8u * (2 * CT_STAGES + 4);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(ct_raw + (holder + 8 - raw));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < CT_STAGES; ++s) {
+      tc::mbar_init(full(s), CT_PRODUCERS + 1);
+      tc::mbar_init(empty(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      tc::mbar_init(acc_full(b), 1);
+      tc::mbar_init(acc_empty(b), 128);
+    }
+    *abort_s = 0;
+    tc::fence_mbar_init();
+    tc::prefetch_tmap(&tmW);
+  }
+  if (warp == 4) tc::tmem_alloc(holder, 512);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(ct_raw + (holder - raw));
+
+  const int total = a.G * a.m_tiles * a.n_tiles;
+
+  if (warp < 4) {
+    // ---------------- gather producers: 4 warps x 32 columns, 32 rows each per stage ---------
+    int kb_global = 0;
+    int pending_stage = -1;
+    for (int t = blockIdx.x; t < total && !*abort_s; t += gridDim.x) {
+      const int nt = t % a.n_tiles;
+      const int mt = (t / a.n_tiles) % a.m_tiles;
+      const int g = t / (a.n_tiles * a.m_tiles);
+      const int col = nt * 32 + lane;
+      const bool col_ok = col < a.L;
+      const int32_t* idx_g = a.idx + (size_t)g * a.K;
+      for (int kb = 0; kb < a.k_blocks; ++kb, ++kb_global) {
+        const int s = kb_global % CT_STAGES;
+        const uint32_t use = (uint32_t)(kb_global / CT_STAGES);
+        if (use > 0 && !ct_wait(empty(s), (use - 1) & 1u, abort_s)) break;
+        const uint32_t a_s = base + s * CT_STAGE_BYTES;
+        const uint32_t b_s = a_s + CT_A_BYTES;
+        if (warp == 0 && lane == 0) {  // the W tile of this stage, by TMA
+          tc::mbar_expect_tx(full(s), CT_A_BYTES);
+          tc::tma_load_2d(a_s, &tmW, kb * CT_BK, mt * CT_BM, full(s));
+        }
+        // this lane's row index for the 32 rows of the warp: k = kb*128 + warp + 4*i
+        const int kr = kb * CT_BK + warp + 4 * lane;
+        const int my_idx = (kr < a.K) ? __ldg(idx_g + kr) : -1;
+        const int box = lane >> 4, ch = (lane & 15) >> 1, half = lane & 1;
+#pragma unroll 4
+        for (int i = 0; i < 32; ++i) {
+          const int r = warp + 4 * i;  // row within the stage
+          const int x = __shfl_sync(0xffffffffu, my_idx, i);
+          const bool ok = col_ok && x >= 0;
+          const uint64_t* src = ok ? a.X + (size_t)x * a.L + col : a.X;
+          const uint32_t dst = b_s + box * (CT_BK * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
+                               ((ch ^ (r & 7)) << 4) + half * 8;
+          cp_async8(dst, src, ok ? 8u : 0u);
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+        // release the previous stage once its copies have landed
+        if (pending_stage >= 0) {
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          tc::mbar_arrive(full(pending_stage));
+        }
+        pending_stage = s;
+      }
+    }
+    if (pending_stage >= 0) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc::mbar_arrive(full(pending_stage));
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issue (one elected lane) --------------------------------------------
+    if (lane == 0) {
+      int kb_global = 0, tt = 0;
+      for (int t = blockIdx.x; t < total && !*abort_s; t += gridDim.x, ++tt) {
+        const int buf = tt & 1;
+        const uint32_t d_tmem = tmem + (uint32_t)(buf * 256);
+        if (tt >= 2 && !ct_wait(acc_empty(buf), (uint32_t)((tt >> 1) - 1) & 1u, abort_s)) break;
+        tc::tc_fence_after();
+        bool ok = true;
+        for (int kb = 0; kb < a.k_blocks; ++kb, ++kb_global) {
+          const int s = kb_global % CT_STAGES;
+          const uint32_t use = (uint32_t)(kb_global / CT_STAGES);
+          const uint32_t a_s = base + s * CT_STAGE_BYTES;
+          if (!ct_wait(full(s), use & 1u, abort_s)) { ok = false; break; }
+          tc::tc_fence_after();
+          const uint32_t b_s = a_s + CT_A_BYTES;
+#pragma unroll
+          for (int k = 0; k < CT_BK / 32; ++k) {
+            const uint64_t ad = tc::smem_desc_sw128(a_s + 32u * k, 16u, 1024u);
+            const uint64_t bd = tc::smem_desc_sw128(b_s + 4096u * k, (uint32_t)(CT_BK * 128),
+                                                    1024u);
+            tc::mma_i8(d_tmem, ad, bd, CT_IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          tc::mma_commit(empty(s));
+        }
+        if (!ok) break;
+        tc::mma_commit(acc_full(buf));
+      }
+    }
+  } else {
+    // ---------------- epilogue: warps 5..8 -> TMEM lane quarters 1, 2, 3, 0 -----------------
+    const int q = warp & 3;
+    int tt = 0;
+    for (int t = blockIdx.x; t < total && !*abort_s; t += gridDim.x, ++tt) {
+      const int nt = t % a.n_tiles;
+      const int mt = (t / a.n_tiles) % a.m_tiles;
+      const int g = t / (a.n_tiles * a.m_tiles);
+      const int buf = tt & 1;
+      if (!ct_wait(acc_full(buf), (uint32_t)(tt >> 1) & 1u, abort_s)) break;
+      tc::tc_fence_after();
+      const int row = mt * CT_BM + q * 32 + lane;
+      const bool row_ok = row < a.M;
+      const uint64_t bterm = (row_ok && a.bias) ? (uint64_t)a.bias[row] * a.delta : 0;
+      uint64_t* yrow = a.Y + ((size_t)g * a.M + (row_ok ? row : 0)) * a.L;
+#pragma unroll 1
+      for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
+        uint32_t r[32];
+        tc::tmem_ld_32x32(tmem + (uint32_t)(buf * 256) + ((uint32_t)(q * 32) << 16) +
+                              (uint32_t)(chunk * 32),
+                          r);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint64_t v = 0;
+#pragma unroll
+          for (int b = 0; b < 8; ++b) v += (uint64_t)(int64_t)(int32_t)r[u * 8 + b] << (8 * b);
+          const int col = nt * 32 + chunk * 4 + u;
+          if (row_ok && col < a.L) yrow[col] = v + (col == a.L - 1 ? bterm : 0);
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(acc_empty(buf));
+    }
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+}
+
+// W int8 [M][K] -> zero-padded [Mp][Kp] (Mp, Kp multiples of 128).
+__global__ void pad_weights_kernel(const int8_t* __restrict__ W, int M, int K, int8_t* Wp,
+                                   int Mp, int Kp) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (size_t)Mp * Kp) return;
+  const int r = (int)(i / Kp), c = (int)(i % Kp);
+  Wp[i] = (r < M && c < K) ? W[(size_t)r * K + c] : (int8_t)0;
+}
+
+// idx[g][k] = g*K + k: the dense (Linear) gather.
+__global__ void dense_index_kernel(int32_t* idx, int G, int K) {
+  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < (size_t)G * K) idx[i] = (int32_t)i;
+}
+
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 148;
+  return n;
+}
+
+int lwe_contract_gather(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                        const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
+                        cudaStream_t st) {
+  if (M <= 0 || K <= 0 || G < 0 || L <= 0 || K > 65536) {
+    set_error("contract: bad shape M=%d K=%d groups=%d L=%d (K <= 65536)", M, K, G, L);
+    return PNB_ERR_INVALID;
+  }
+  if (G == 0) return PNB_OK;
+  const int Mp = (M + CT_BM - 1) / CT_BM * CT_BM, Kp = (K + CT_BK - 1) / CT_BK * CT_BK;
+  int8_t* Wp = nullptr;
+  PNB_CUDA(cudaMallocAsync((void**)&Wp, (size_t)Mp * Kp, st));
+  const size_t nw = (size_t)Mp * Kp;
+  pad_weights_kernel<<<(unsigned)((nw + 255) / 256), 256, 0, st>>>(W, M, K, Wp, Mp, Kp);
+  int rc = PNB_OK;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) rc = cuda_status(e, "pad_weights_kernel");
+  CUtensorMap tmW;
+  if (rc == PNB_OK) rc = make_tmap_u8_2d(&tmW, Wp, (uint64_t)Kp, (uint64_t)Mp, (uint64_t)Kp,
+                                         CT_BK, CT_BM);
+  if (rc == PNB_OK) {
+    static bool attr_done[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+      e = cudaFuncSetAttribute(contract_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               CT_SMEM);
+      if (e != cudaSuccess) rc = cuda_status(e, "cudaFuncSetAttribute(contract)");
+      else attr_done[dev] = true;
+    }
+  }
+  if (rc == PNB_OK) {
+    CtArgs args;
+    args.X = X; args.idx = idx; args.bias = bias; args.Y = Y; args.delta = delta;
+    args.G = G; args.M = M; args.K = K; args.L = L;
+    args.m_tiles = Mp / CT_BM;
+    args.n_tiles = (8 * L + CT_BN - 1) / CT_BN;
+    args.k_blocks = Kp / CT_BK;
+    const long long tiles = (long long)G * args.m_tiles * args.n_tiles;
+    if (tiles > 0x7fffffffLL) {
+      set_error("contract: %lld tiles exceed one launch", tiles);
+      rc = PNB_ERR_INVALID;
+    } else {
+      const int grid = (int)std::min<long long>(tiles, (long long)sm_count());
+      contract_tc_kernel<<<grid, CT_THREADS, CT_SMEM, st>>>(tmW, args);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) rc = cuda_status(e, "contract_tc_kernel");
+    }
+  }
+  e = cudaFreeAsync(Wp, st);
+  if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(padded weights)");
+  return rc;
+}
+
+int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                    const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st) {
+  if (batch <= 0) return batch == 0 ? PNB_OK : PNB_ERR_INVALID;
+  int32_t* idx = nullptr;
+  PNB_CUDA(cudaMallocAsync((void**)&idx, sizeof(int32_t) * (size_t)batch * K, st));
+  const size_t n = (size_t)batch * K;
+  dense_index_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(idx, batch, K);
+  int rc = PNB_OK;
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) rc = cuda_status(e, "dense_index_kernel");
+  if (rc == PNB_OK) rc = lwe_contract_gather(W, bias, delta, M, K, X, idx, batch, Y, L, st);
+  e = cudaFreeAsync(idx, st);
+  if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(index)");
+  return rc;
+}
+
+}  // namespace pnb

@@ -42,6 +42,11 @@ int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count,
 int lwe_contract(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                  const uint64_t* X, uint64_t* Y, int batch, int lwe_len, cudaStream_t st);
 int measure_fp64_peak(double* tflops);
+int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                    const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st);
+int lwe_contract_gather(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                        const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
+                        cudaStream_t st);
 int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count, void* digits,
                  cudaStream_t st);
 size_t ks_tc_workspace_bytes(const pnb_params& p, int count);
@@ -50,4 +55,5 @@ bool fft_tables_ready();
 int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
                       int count, cudaStream_t st);
 int br_status_read_and_clear(int* out);
+int ct_status_read_and_clear(int* out);
 }  // namespace pnb

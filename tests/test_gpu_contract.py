@@ -15,9 +15,11 @@ pytestmark = pytest.mark.gpu
 
 @pytest.mark.parametrize("M,K,B,L,with_bias", [
     (10, 36, 3, 2049, True),     # tiny-CNN head (36 -> 10) at N = 2048
-    (128, 784, 2, 2049, True),   # 784 -> 128 layer
+    (128, 784, 2, 2049, True),   # 784 -> 128 layer (7 K blocks through 4 pipeline stages)
     (33, 65, 1, 300, False),     # ragged tiles, no bias
     (1, 1, 1, 1, True),          # degenerate
+    (200, 130, 3, 2049, True),   # two M tiles; 390 tiles over the persistent CTAs
+    (16, 72, 9, 2049, False),    # 585 tiles: several per CTA, both TMEM buffers reused
 ])
 def test_contract_bit_exact(pnb, oracle, M, K, B, L, with_bias):
     rng = np.random.default_rng(M * 1000 + K)
@@ -49,3 +51,39 @@ def test_contract_decrypts_to_integer_linear_layer(pnb):
     ph = pnb.phase(keys, Y.reshape(B * M, -1)).cpu().numpy()
     dec = np.round(ph.astype(np.float64) / delta).astype(np.int64).reshape(B, M)
     assert np.array_equal(dec, x @ W.T + bias)
+
+
+def test_contract_gather_matches_im2col(pnb, oracle):
+    # A 2x2 / stride-1 "convolution" over a 1 x 5 x 5 map of ciphertexts with zero padding 1:
+    # the gather table holds, per output position, the input ciphertext under each tap.
+    rng = np.random.default_rng(77)
+    H = W_ = 5
+    L = 2049
+    X = rng.integers(0, 1 << 63, (H * W_, L), dtype=np.uint64) * np.uint64(2)
+    kh = kw = 2
+    pad = 1
+    oh, ow = H + 2 * pad - kh + 1, W_ + 2 * pad - kw + 1
+    idx = np.full((oh * ow, kh * kw), -1, dtype=np.int32)
+    for oy in range(oh):
+        for ox in range(ow):
+            for ky in range(kh):
+                for kx in range(kw):
+                    iy, ix = oy + ky - pad, ox + kx - pad
+                    if 0 <= iy < H and 0 <= ix < W_:
+                        idx[oy * ow + ox, ky * kw + kx] = iy * W_ + ix
+    Wt = rng.integers(-8, 8, (3, kh * kw), dtype=np.int64)
+    bias = rng.integers(-20, 20, 3)
+    delta = 1 << 50
+    got = pnb.lwe_contract_gather(torch.tensor(Wt.astype(np.int8), device="cuda"),
+                                  torch.tensor(bias, device="cuda"), delta,
+                                  torch.tensor(X.view(np.int64), device="cuda"),
+                                  torch.tensor(idx, device="cuda"))
+    got = got.cpu().numpy().view(np.uint64)
+    Xg = np.zeros((oh * ow, kh * kw, L), dtype=np.uint64)
+    for g in range(oh * ow):
+        for k in range(kh * kw):
+            if idx[g, k] >= 0:
+                Xg[g, k] = X[idx[g, k]]
+    want = oracle.contract(Wt, bias, delta, Xg)
+    assert np.array_equal(got, want)
+    assert pnb.device_status(0) == 0
