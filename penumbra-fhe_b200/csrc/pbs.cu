@@ -366,22 +366,164 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 
 constexpr int BR_CPB = 4;
 
+// ------------------------------------------------------------------------------------------
+// Blind rotation with pbs_level = L >= 2 (the low-noise bootstrap whose outputs feed another
+// contraction).  One block of 2 warps per ciphertext; warp p owns GLWE polynomial p.  The
+// accumulator keeps all 64 bits (L levels read up to L*base_log bits of it); for each level the
+// two warps transform their digit polynomials, exchange the spectra and accumulate their output
+// polynomial's spectrum in shared memory; one inverse FFT per warp closes the iteration.
+// ------------------------------------------------------------------------------------------
+struct BrMlSmem {
+  uint64_t acc[2][FFT_N];
+  double2 facc[2][FFT_M];
+  double2 xbuf[2][FFT_M];
+  uint16_t abar[BR_MAXN];
+};
+
+// Digit `lev` (0 = most significant) of the signed gadget decomposition of v.
+template <int L>
+__device__ __forceinline__ int64_t gadget_digit(uint64_t v, int beta, int lev) {
+  const int total = beta * L;
+  uint64_t st = (v >> (64 - total)) + ((v >> (63 - total)) & 1u);
+  const uint64_t mask = (1ull << beta) - 1, half = 1ull << (beta - 1);
+  int64_t d = 0;
+#pragma unroll
+  for (int j = L - 1; j >= 0; --j) {
+    const uint64_t x = st & mask;
+    st >>= beta;
+    const bool neg = x >= half;
+    if (j == lev) d = neg ? (int64_t)x - (int64_t)(1ull << beta) : (int64_t)x;
+    st += neg ? 1u : 0u;
+  }
+  return d;
+}
+
+template <int L>
+__global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
+    const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
+    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
+    int base_log, FftTables tb) {
+  extern __shared__ __align__(16) unsigned char ml_raw[];
+  BrMlSmem& S = *reinterpret_cast<BrMlSmem*>(ml_raw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ct = blockIdx.x;
+  const uint64_t* in = small_ct + (size_t)ct * (n + 1);
+  constexpr int LG = 12;
+  for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
+  const int bt = modswitch(in[n], LG);
+  const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
+  for (int t = threadIdx.x; t < FFT_N; t += 64) {
+    S.acc[0][t] = 0;
+    S.acc[1][t] = rot_coef(tv, t, r0);
+  }
+  __syncthreads();
+  uint64_t* my = S.acc[warp];
+  double2* buf = S.xbuf[warp];
+  const double2* obuf = S.xbuf[warp ^ 1];
+  double2* facc = S.facc[warp];
+  constexpr int ROWS = 2 * L;
+
+  for (int i = 0; i < n; ++i) {
+    const int a = S.abar[i];
+    if (a == 0) continue;  // X^0 - 1 = 0: the CMux leaves the accumulator unchanged
+    const double2* ggsw = fbsk + (size_t)i * ROWS * 2 * FFT_M;
+    for (int lev = 0; lev < L; ++lev) {
+      double2 x[FFT_R];
+#pragma unroll
+      for (int m = 0; m < 32; ++m) {
+        if ((m & 7) == 0) asm volatile("" ::: "memory");
+        const int j = lane + 32 * m;
+        const uint64_t v0 = rot_coef(my, j, a) - my[j];
+        const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
+        x[m] = make_double2((double)gadget_digit<L>(v0, base_log, lev),
+                            (double)gadget_digit<L>(v1, base_log, lev));
+      }
+      fft_forward(x, buf, lane, tb);
+#pragma unroll
+      for (int r = 0; r < 32; ++r) buf[r * 32 + lane] = x[r];
+      __syncthreads();
+      // output polynomial `warp`: rows (warp, lev) and (other, lev) of the GGSW
+      const double2* f_own = ggsw + ((size_t)(warp * L + lev) * 2 + warp) * FFT_M;
+      const double2* f_oth = ggsw + ((size_t)((warp ^ 1) * L + lev) * 2 + warp) * FFT_M;
+#pragma unroll
+      for (int r = 0; r < 32; ++r) {
+        if ((r & 7) == 0) asm volatile("" ::: "memory");
+        const int e = r * 32 + lane;
+        const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
+        const double2 dt = obuf[e];
+        const double2 p0 = cmul(x[r], fo);
+        double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
+                                 p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+        if (lev > 0) {
+          const double2 o = facc[e];
+          v = make_double2(v.x + o.x, v.y + o.y);
+        }
+        facc[e] = v;
+      }
+      __syncthreads();
+    }
+    double2 x[FFT_R];
+#pragma unroll
+    for (int r = 0; r < 32; ++r) x[r] = facc[r * 32 + lane];
+    fft_inverse(x, buf, lane, tb);
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      if ((m & 7) == 0) asm volatile("" ::: "memory");
+      const int j = lane + 32 * m;
+      my[j] += f64_to_torus(x[m].x);
+      my[j + FFT_M] += f64_to_torus(x[m].y);
+    }
+    __syncthreads();
+  }
+  uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+  for (int t = threadIdx.x; t < FFT_N; t += 64)
+    o[t] = (t == 0) ? S.acc[0][0] : (uint64_t)0 - S.acc[0][FFT_N - t];
+  if (threadIdx.x == 0) o[FFT_N] = S.acc[1][0];
+}
+
+template <int L>
+static int launch_ml(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
+                     uint64_t* out, int count, FftTables tb, cudaStream_t st) {
+  const int smem = sizeof(BrMlSmem);
+  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_ml_kernel<L>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  blind_rotate_ml_kernel<L><<<count, 64, smem, st>>>(small, tv, K->fbsk, out, count, K->p.n,
+                                                     K->p.pbs_base_log, tb);
+  PNB_CHECK_LAUNCH("blind_rotate_ml_kernel");
+  return PNB_OK;
+}
+
 static bool br_supported(const pnb_params& p) {
-  return p.k == 1 && p.N == FFT_N && p.pbs_level == 1 && p.n <= BR_MAXN && p.n > 0 &&
-         p.pbs_base_log >= 2 && p.pbs_base_log <= 40;
+  if (p.k != 1 || p.N != FFT_N || p.n > BR_MAXN || p.n <= 0) return false;
+  if (p.pbs_level == 1) return p.pbs_base_log >= 2 && p.pbs_base_log <= 30;
+  // multi-level: digits below 2^22 in magnitude keep the f64 product's error small
+  return p.pbs_level >= 2 && p.pbs_level <= 6 && p.pbs_base_log >= 2 &&
+         p.pbs_base_log <= 22 && p.pbs_base_log * p.pbs_level < 64;
 }
 
 int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
                         uint64_t* out, int count, cudaStream_t st) {
   if (!br_supported(K->p)) {
-    set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level=1, n<=%d (got "
-              "k=%d N=%d level=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level, K->p.n);
+    set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level 1..6, n<=%d (got "
+              "k=%d N=%d level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
+              K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
   }
   if (count <= 0) return PNB_OK;
   FftTables tb;
   int rc = fft_tables_get(&tb);
   if (rc) return rc;
+  switch (K->p.pbs_level) {
+    case 1: break;
+    case 2: return launch_ml<2>(K, tv, small, out, count, tb, st);
+    case 3: return launch_ml<3>(K, tv, small, out, count, tb, st);
+    case 4: return launch_ml<4>(K, tv, small, out, count, tb, st);
+    case 5: return launch_ml<5>(K, tv, small, out, count, tb, st);
+    case 6: return launch_ml<6>(K, tv, small, out, count, tb, st);
+    default:
+      set_error("blind rotation: pbs_level %d not compiled", K->p.pbs_level);
+      return PNB_ERR_UNSUPPORTED;
+  }
   constexpr int smem = BrLayout<BR_CPB>::BYTES;
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_kernel<BR_CPB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
@@ -403,8 +545,9 @@ size_t pbs_workspace_bytes(const pnb_keys* K, int count) {
 int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
               int count, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!br_supported(K->p)) {
-    set_error("pbs: compiled kernels cover k=1, N=2048, pbs_level=1, n<=%d (got k=%d N=%d "
-              "level=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level, K->p.n);
+    set_error("pbs: compiled kernels cover k=1, N=2048, pbs_level 1..6, n<=%d (got k=%d N=%d "
+              "level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
+              K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
   }
   if (count == 0) return PNB_OK;

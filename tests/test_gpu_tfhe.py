@@ -164,3 +164,30 @@ def test_pbs_argument_errors(pnb, gkeys):
         pnb.pbs_batch(gkeys, tv, ct, workspace=small)
     with pytest.raises(pnb.LibraryError):
         pnb.test_vector(gkeys, list(range(3)))  # does not divide N
+
+
+@pytest.mark.parametrize("beta,level", [(15, 2), (7, 6)])
+def test_multilevel_bootstrap(pnb, oracle, beta, level):
+    """Low-noise bootstrap (more gadget levels, same secret keys and keyswitching key)."""
+    p = pnb.default_params()
+    p.pbs_base_log, p.pbs_level = beta, level
+    keys = pnb.keygen(p, seed=SEED, device=0)
+    op = oracle.default_params()
+    op.pbs_base_log, op.pbs_level = beta, level
+    ok = oracle.OracleKeys(op, seed=SEED)
+    ex = keys.export(lwe_sk=True, glwe_sk=True, bsk=True)
+    assert np.array_equal(ex["bsk"], ok.bsk)
+    rng = np.random.default_rng(level)
+    msgs = rng.integers(0, 16, 512)
+    lut = rng.integers(0, 16, 16)
+    tv = pnb.test_vector(keys, lut)
+    ct = pnb.encrypt(keys, torch.tensor(msgs), seed=11)
+    out = pnb.pbs_batch(keys, tv, ct)
+    assert np.array_equal(pnb.decrypt_vec(keys, out).cpu().numpy(), lut[msgs])
+    gpu_noise = _noise(_u64(pnb.phase(keys, out)), lut[msgs], p.delta())
+    ref = ok.pbs_fft(_u64(ct[:64]), ok.test_vector(lut))
+    ref_noise = _noise(ok.phase_big(ref), lut[msgs[:64]], p.delta())
+    ratio = gpu_noise.var() / ref_noise.var()
+    assert 0.5 < ratio < 2.0, f"noise variance ratio {ratio:.3f}"
+    # the whole point of the extra levels: far below the one-level set's ~2^49
+    assert np.log2(gpu_noise.std()) < {2: 43.5, 6: 35.0}[level]
