@@ -166,6 +166,72 @@ int pnb_device_status(int device, int* status_out);
  * roofline denominator of the blind rotation.  No reference counterpart. */
 int pnb_measure_fp64_peak(int device, double* tflops_out);
 
+/* ---- Graph evaluation ------------------------------------------------------------------
+ * The IR graph (a model.fhe document), compiled into a batched ciphertext program and run on
+ * one GPU.  Every tensor element is one big-key LWE ciphertext holding the exact integer at a
+ * per-tensor power-of-two scale (pnb_plan_tensor); Requant, Activation and Argmax are exact
+ * bootstrap programs whose decrypted outputs equal the reference's integer semantics. */
+typedef struct pnb_graph pnb_graph;
+typedef struct pnb_plan pnb_plan;
+typedef struct pnb_evaluator pnb_evaluator;
+
+typedef struct pnb_plan_summary {
+  int64_t input_elems;     /* ciphertexts per sample over all graph inputs, in graph order */
+  int64_t output_elems;    /* ciphertexts per sample over all graph outputs, in graph order */
+  int32_t num_inputs, num_outputs;
+  int64_t pbs_per_sample;  /* bootstraps one sample costs */
+  double cost_per_sample;  /* the same in single-level bootstrap equivalents */
+  int32_t num_instructions;
+  int32_t reserved;
+} pnb_plan_summary;
+
+/* Parse and validate a graph document (the graph object itself, or a document holding it under
+ * "graph").  Same schema gate and op validation as the reference, with its messages.
+ * Replaces: Graph::from_json + OpSpec::build (runtime/src/ir.rs:169-180, 197-452). */
+int pnb_graph_load(const char* json, size_t len, pnb_graph** out);
+int pnb_graph_free(pnb_graph* graph);
+int pnb_graph_info(const pnb_graph* graph, int* num_nodes, int* num_blocks, int* input_bits);
+
+/* Bit-width budget of the graph against its num_blocks radix (PNB_ERR_INVALID + message when
+ * exceeded).  Replaces: check_graph_bit_width_budget (runtime/src/eval.rs:237-276). */
+int pnb_graph_check_budget(const pnb_graph* graph);
+
+/* Compile a graph for a parameter set.  input_lens (may be NULL; one entry per graph input, 0 =
+ * infer from the consumer) gives the element count of each graph input; input_lo/input_hi bound
+ * every graph-input value; margin_sigmas (<= 0: 7) is the decision margin of every bootstrap in
+ * noise standard deviations.  Fails when the graph exceeds the budget or no exact program
+ * exists.  Replaces: the per-node op construction of evaluate_graph (runtime/src/eval.rs:94-133). */
+int pnb_plan_create(const pnb_graph* graph, const pnb_params* params, const int64_t* input_lens,
+                    int64_t input_lo, int64_t input_hi, double margin_sigmas, pnb_plan** out);
+int pnb_plan_free(pnb_plan* plan);
+int pnb_plan_info(const pnb_plan* plan, pnb_plan_summary* info);
+/* Element count, plaintext scale (log2) and value range of input (is_output = 0) or output
+ * tensor idx.  Encrypt inputs at 2^scale_log2; decode outputs by signed rounding at 2^scale_log2. */
+int pnb_plan_tensor(const pnb_plan* plan, int is_output, int idx, int64_t* elems,
+                    int* scale_log2, int64_t* lo, int64_t* hi);
+/* Human-readable program summary (bytes needed including the terminator). */
+size_t pnb_plan_report(const pnb_plan* plan, char* buf, size_t cap);
+/* Noise-free host execution of the program on cleartext integers: inputs [batch][input_elems],
+ * outputs [batch][output_elems]; min_margin (may be NULL) receives the smallest distance, in
+ * units of 2^64/2N, from a bootstrap input to a decision boundary.  No GPU needed. */
+int pnb_plan_simulate(const pnb_plan* plan, const int64_t* inputs, int batch, int64_t* outputs,
+                      double* min_margin);
+
+/* Create the GPU evaluator of a plan: generates on `device` every bootstrapping key set the
+ * program uses from `seed` (all share the secret keys and the keyswitching key) and uploads the
+ * program tables.  max_bytes bounds the per-chunk ciphertext buffers (0: half the free memory).
+ * Replaces: keys::keygen + EvalCtx (runtime/src/keys.rs:47-56, ops/mod.rs:64-69). */
+int pnb_evaluator_create(const pnb_plan* plan, int device, uint64_t seed, size_t max_bytes,
+                         pnb_evaluator** out);
+int pnb_evaluator_free(pnb_evaluator* ev);
+/* The evaluator's client key set (borrowed): encrypt inputs / decrypt outputs with it. */
+int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys);
+/* Evaluate `batch` samples: in_dev [batch][input_elems][kN+1], out_dev
+ * [batch][output_elems][kN+1] ciphertexts, on the evaluator's device.
+ * Replaces: evaluate_graph (runtime/src/eval.rs:86-166), batched over samples. */
+int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t* out_dev,
+                 void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -20,7 +20,7 @@ __all__ = [
     "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
-    "device_status", "pbs_batch_noalloc",
+    "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -87,6 +87,26 @@ _SIGS = {
                                          C.c_int, C.c_void_p]),
     "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
     "pnb_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
+    "pnb_graph_load": (C.c_int, [C.c_char_p, C.c_size_t, C.POINTER(C.c_void_p)]),
+    "pnb_graph_free": (C.c_int, [C.c_void_p]),
+    "pnb_graph_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                 C.POINTER(C.c_int)]),
+    "pnb_graph_check_budget": (C.c_int, [C.c_void_p]),
+    "pnb_plan_create": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
+                                  C.c_double, C.POINTER(C.c_void_p)]),
+    "pnb_plan_free": (C.c_int, [C.c_void_p]),
+    "pnb_plan_info": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "pnb_plan_tensor": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.POINTER(C.c_int64),
+                                  C.POINTER(C.c_int), C.POINTER(C.c_int64),
+                                  C.POINTER(C.c_int64)]),
+    "pnb_plan_report": (C.c_size_t, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    "pnb_plan_simulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                    C.POINTER(C.c_double)]),
+    "pnb_evaluator_create": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_size_t,
+                                       C.POINTER(C.c_void_p)]),
+    "pnb_evaluator_free": (C.c_int, [C.c_void_p]),
+    "pnb_evaluator_keys": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "pnb_evaluate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
 _LIB = None
@@ -136,11 +156,13 @@ def default_params() -> Params:
 class KeySet:
     """Keys resident on one GPU (``pnb_keys``): Fourier BSK, KSK and client secrets."""
 
-    def __init__(self, handle: C.c_void_p, params: Params, device: int, seed: int):
+    def __init__(self, handle: C.c_void_p, params: Params, device: int, seed: int,
+                 owner=None):
         self._h = handle
         self.params = params
         self.device = device
         self.seed = seed
+        self._owner = owner  # a borrowed key set keeps its owner alive and never frees
 
     @property
     def handle(self) -> C.c_void_p:
@@ -149,9 +171,9 @@ class KeySet:
         return self._h
 
     def free(self):
-        if self._h:
+        if self._h and self._owner is None:
             lib().pnb_keys_free(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:
@@ -399,3 +421,168 @@ def measure_fp64_peak(device: int = 0) -> float:
     v = C.c_double()
     _check("pnb_measure_fp64_peak", lib().pnb_measure_fp64_peak(device, C.byref(v)))
     return v.value
+
+
+# ---- graph evaluation ------------------------------------------------------------------------
+
+class _PlanSummary(C.Structure):
+    _fields_ = [("input_elems", C.c_int64), ("output_elems", C.c_int64),
+                ("num_inputs", C.c_int32), ("num_outputs", C.c_int32),
+                ("pbs_per_sample", C.c_int64), ("cost_per_sample", C.c_double),
+                ("num_instructions", C.c_int32), ("reserved", C.c_int32)]
+
+
+class Graph:
+    """An IR graph (``model.fhe``), parsed and validated by the library.
+
+    Mirrors ``Graph::from_json`` + ``OpSpec::build`` (runtime/src/ir.rs:169-180, 197-452);
+    errors raise ``LibraryError`` carrying the reference's diagnosis."""
+
+    def __init__(self, doc):
+        import json as _json
+        if isinstance(doc, dict):
+            doc = _json.dumps(doc)
+        if isinstance(doc, str):
+            doc = doc.encode()
+        h = C.c_void_p()
+        _check("pnb_graph_load", lib().pnb_graph_load(doc, len(doc), C.byref(h)))
+        self._h = h
+
+    def check_budget(self):
+        """``check_graph_bit_width_budget`` (runtime/src/eval.rs:237-276)."""
+        _check("pnb_graph_check_budget", lib().pnb_graph_check_budget(self._h))
+
+    def info(self) -> dict:
+        a, b, c = C.c_int(), C.c_int(), C.c_int()
+        _check("pnb_graph_info", lib().pnb_graph_info(self._h, C.byref(a), C.byref(b), C.byref(c)))
+        return {"num_nodes": a.value, "num_blocks": b.value, "input_bits": c.value}
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().pnb_graph_free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+class Plan:
+    """A graph compiled into a batched ciphertext program (host only; no GPU needed)."""
+
+    def __init__(self, graph: Graph, params: Params | None = None, input_range=None,
+                 margin_sigmas: float = 0.0, input_lens=None):
+        import numpy as np
+        self.params = default_params() if params is None else params
+        if input_range is None:
+            bits = graph.info()["input_bits"]
+            input_range = (0, (1 << bits) - 1)
+        lens = None
+        if input_lens is not None:
+            lens = np.ascontiguousarray(np.asarray(input_lens, dtype=np.int64))
+        h = C.c_void_p()
+        _check("pnb_plan_create",
+               lib().pnb_plan_create(graph._h, C.byref(self.params),
+                                     C.c_void_p(0) if lens is None else C.c_void_p(lens.ctypes.data),
+                                     int(input_range[0]), int(input_range[1]),
+                                     float(margin_sigmas), C.byref(h)))
+        self._h = h
+        s = _PlanSummary()
+        _check("pnb_plan_info", lib().pnb_plan_info(h, C.byref(s)))
+        self.input_elems = s.input_elems
+        self.output_elems = s.output_elems
+        self.pbs_per_sample = s.pbs_per_sample
+        self.cost_per_sample = s.cost_per_sample
+        self.num_instructions = s.num_instructions
+        self.inputs = [self._tensor(0, i) for i in range(s.num_inputs)]
+        self.outputs = [self._tensor(1, i) for i in range(s.num_outputs)]
+
+    def _tensor(self, is_out, i):
+        e, sc, lo, hi = C.c_int64(), C.c_int(), C.c_int64(), C.c_int64()
+        _check("pnb_plan_tensor", lib().pnb_plan_tensor(self._h, is_out, i, C.byref(e),
+                                                        C.byref(sc), C.byref(lo), C.byref(hi)))
+        return {"elems": e.value, "scale": sc.value, "lo": lo.value, "hi": hi.value}
+
+    def report(self) -> str:
+        n = lib().pnb_plan_report(self._h, None, 0)
+        buf = C.create_string_buffer(n)
+        lib().pnb_plan_report(self._h, buf, n)
+        return buf.value.decode()
+
+    def simulate(self, x):
+        """Noise-free host execution on integers [batch][input_elems] -> (outputs, margin)."""
+        import numpy as np
+        x = np.ascontiguousarray(np.asarray(x, dtype=np.int64).reshape(-1, self.input_elems))
+        y = np.zeros((x.shape[0], self.output_elems), dtype=np.int64)
+        m = C.c_double()
+        _check("pnb_plan_simulate",
+               lib().pnb_plan_simulate(self._h, C.c_void_p(x.ctypes.data), x.shape[0],
+                                       C.c_void_p(y.ctypes.data), C.byref(m)))
+        return y, m.value
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().pnb_plan_free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+class Evaluator:
+    """A plan bound to one GPU with its key sets (``EvalCtx`` + ``evaluate_graph``)."""
+
+    def __init__(self, plan: Plan, device: int = 0, seed: int = 0, max_bytes: int = 0):
+        self.plan = plan
+        self.device = device
+        h = C.c_void_p()
+        _check("pnb_evaluator_create",
+               lib().pnb_evaluator_create(plan._h, device, seed, max_bytes, C.byref(h)))
+        self._h = h
+        k = C.c_void_p()
+        _check("pnb_evaluator_keys", lib().pnb_evaluator_keys(h, C.byref(k)))
+        self.keys = KeySet(k, plan.params, device, seed, owner=self)
+        self.row = plan.params.k * plan.params.N + 1
+
+    def encrypt(self, x, seed: int = 1, first_index: int = 0) -> torch.Tensor:
+        """Encrypt integers [batch][input_elems] at each input tensor's scale."""
+        dev = torch.device("cuda", self.device)
+        x = torch.as_tensor(x, dtype=torch.int64).reshape(-1, self.plan.input_elems)
+        B = x.shape[0]
+        ct = torch.empty((B, self.plan.input_elems, self.row), dtype=torch.int64, device=dev)
+        off = 0
+        for t in self.plan.inputs:
+            e = t["elems"]
+            part = encrypt(self.keys, x[:, off:off + e].reshape(-1), seed,
+                           first_index + off * B, delta=1 << t["scale"])
+            ct[:, off:off + e] = part.reshape(B, e, self.row)
+            off += e
+        return ct
+
+    def evaluate(self, ct: torch.Tensor) -> torch.Tensor:
+        ct = _u64(ct).contiguous()
+        B = ct.numel() // (self.plan.input_elems * self.row)
+        out = torch.empty((B, self.plan.output_elems, self.row), dtype=torch.int64,
+                          device=ct.device)
+        _check("pnb_evaluate", lib().pnb_evaluate(self._h, _ptr(ct), B, _ptr(out),
+                                                  _stream(ct.device)))
+        return out
+
+    def decrypt(self, out: torch.Tensor) -> torch.Tensor:
+        """Decode [batch][output_elems] signed integers at each output tensor's scale."""
+        B = out.shape[0]
+        ph = phase(self.keys, out.reshape(-1, self.row)).reshape(B, self.plan.output_elems)
+        res = torch.empty_like(ph)
+        off = 0
+        for t in self.plan.outputs:
+            e, s = t["elems"], t["scale"]
+            res[:, off:off + e] = torch.bitwise_right_shift(ph[:, off:off + e] + (1 << (s - 1)), s)
+            off += e
+        return res
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().pnb_evaluator_free(self._h)
+                self._h = None
+        except Exception:
+            pass

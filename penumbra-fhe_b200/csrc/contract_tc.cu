@@ -61,9 +61,10 @@ struct CtArgs {
   const uint64_t* X;       // ciphertexts [*][L]
   const int32_t* idx;      // [G][K] ciphertext index into X, -1 = zero
   const int64_t* bias;     // [M] or null
-  uint64_t* Y;             // [G][M][L]
+  uint64_t* Y;             // [G][M][L], or [G/P][M][P][L] when P > 0
   uint64_t delta;
   int G, M, K, L;
+  int P;                   // output positions per sample (channel-major placement); 0 = off
   int m_tiles, n_tiles, k_blocks;
 };
 
@@ -213,7 +214,10 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
       const int row = mt * CT_BM + q * 32 + lane;
       const bool row_ok = row < a.M;
       const uint64_t bterm = (row_ok && a.bias) ? (uint64_t)a.bias[row] * a.delta : 0;
-      uint64_t* yrow = a.Y + ((size_t)g * a.M + (row_ok ? row : 0)) * a.L;
+      const int r_ = row_ok ? row : 0;
+      const size_t yr = a.P > 0 ? ((size_t)(g / a.P) * a.M + r_) * a.P + (g % a.P)
+                                : (size_t)g * a.M + r_;
+      uint64_t* yrow = a.Y + yr * a.L;
 #pragma unroll 1
       for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
         uint32_t r[32];
@@ -266,6 +270,16 @@ static int sm_count() {
 int lwe_contract_gather(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                         const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
                         cudaStream_t st) {
+  return lwe_contract_gather_placed(W, bias, delta, M, K, X, idx, G, Y, L, 0, st);
+}
+
+int lwe_contract_gather_placed(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
+                               const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
+                               int P, cudaStream_t st) {
+  if (P < 0 || (P > 0 && G % P != 0)) {
+    set_error("contract: %d groups are not a whole number of samples of %d positions", G, P);
+    return PNB_ERR_INVALID;
+  }
   if (M <= 0 || K <= 0 || G < 0 || L <= 0 || K > 65536) {
     set_error("contract: bad shape M=%d K=%d groups=%d L=%d (K <= 65536)", M, K, G, L);
     return PNB_ERR_INVALID;
@@ -296,7 +310,7 @@ int lwe_contract_gather(const int8_t* W, const int64_t* bias, uint64_t delta, in
   if (rc == PNB_OK) {
     CtArgs args;
     args.X = X; args.idx = idx; args.bias = bias; args.Y = Y; args.delta = delta;
-    args.G = G; args.M = M; args.K = K; args.L = L;
+    args.G = G; args.M = M; args.K = K; args.L = L; args.P = P;
     args.m_tiles = Mp / CT_BM;
     args.n_tiles = (8 * L + CT_BN - 1) / CT_BN;
     args.k_blocks = Kp / CT_BK;

@@ -1,0 +1,622 @@
+// evaluator.cu -- batched execution of a compiled graph program on one GPU, and the graph /
+// plan / evaluator entry points of the C ABI.
+//
+// Replaces the reference's per-sample node walk (runtime/src/eval.rs:86-166): the program built
+// by plan.cpp runs once per chunk of samples, every instruction over the whole chunk.  Buffers
+// are [sample][element][kN+1] u64 big-key LWE ciphertexts; the per-element tables (weights,
+// gather indices, linear-combination coefficients, test-vector choices) are uploaded once.
+#include <algorithm>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "pnb_internal.cuh"
+#include "pnb_keys.h"
+#include "plan.hpp"
+
+struct pnb_graph {
+  pnb::ir::Graph g;
+};
+
+struct pnb_plan {
+  pnb::plan::Program prog;
+  pnb_params params;
+};
+
+namespace pnb {
+namespace {
+
+constexpr int LIN_TERMS = 4;
+constexpr int64_t PBS_SLICE = 1 << 16;  // ciphertexts per keyswitch / rotation launch
+
+struct LinArgs {
+  uint64_t* dst;
+  int64_t E, rows;  // elements per sample, rows = batch * E
+  int L, nt;
+  const uint64_t* src[LIN_TERMS];
+  int64_t srcE[LIN_TERMS];
+  const int64_t* coef[LIN_TERMS];
+  int64_t coef_u[LIN_TERMS];
+  const int32_t* map[LIN_TERMS];
+  const uint64_t* cst;
+  uint64_t cst_u;
+};
+
+// dst[b][e][c] = sum_t coef_t[e] * src_t[b][map_t[e]][c]  (+ cst[e] on the body c = L-1)
+__global__ void __launch_bounds__(256) lin_kernel(LinArgs a) {
+  const int64_t row = blockIdx.x * 2ll + (threadIdx.x >> 7);
+  if (row >= a.rows) return;
+  const int64_t b = row / a.E, e = row - b * a.E;
+  const uint64_t* s[LIN_TERMS];
+  uint64_t k[LIN_TERMS];
+#pragma unroll
+  for (int t = 0; t < LIN_TERMS; ++t) {
+    s[t] = nullptr;
+    k[t] = 0;
+    if (t < a.nt) {
+      const int64_t m = a.map[t] ? a.map[t][e] : e;
+      if (m >= 0) {
+        s[t] = a.src[t] + ((size_t)b * a.srcE[t] + m) * a.L;
+        k[t] = (uint64_t)(a.coef[t] ? a.coef[t][e] : a.coef_u[t]);
+      }
+    }
+  }
+  const uint64_t body = a.cst ? a.cst[e] : a.cst_u;
+  uint64_t* d = a.dst + (size_t)row * a.L;
+  for (int c = threadIdx.x & 127; c < a.L; c += 128) {
+    uint64_t v = (c == a.L - 1) ? body : 0;
+#pragma unroll
+    for (int t = 0; t < LIN_TERMS; ++t)
+      if (s[t]) v += k[t] * s[t][c];
+    d[c] = v;
+  }
+}
+
+// idx[b*P + p][k] = b * Ein + table[p][k]  (-1 stays -1)
+__global__ void gather_batch_kernel(const int32_t* table, int P, int K, int64_t Ein, int batch,
+                                    int32_t* idx) {
+  const int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x;
+  const int64_t n = (int64_t)batch * P * K;
+  if (i >= n) return;
+  const int64_t b = i / ((int64_t)P * K), r = i - b * P * K;
+  const int32_t v = table[r];
+  idx[i] = v < 0 ? -1 : (int32_t)(b * Ein + v);
+}
+
+template <typename T>
+int upload(const std::vector<T>& v, T** out) {
+  *out = nullptr;
+  if (v.empty()) return PNB_OK;
+  PNB_CUDA(cudaMalloc((void**)out, v.size() * sizeof(T)));
+  PNB_CUDA(cudaMemcpy(*out, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+  return PNB_OK;
+}
+
+struct DevInstr {
+  // Lin
+  const int64_t* coef[LIN_TERMS] = {};
+  const int32_t* map[LIN_TERMS] = {};
+  const uint64_t* cst = nullptr;
+  // Pbs
+  const int32_t* tv = nullptr;
+  // Contract
+  const int8_t* W = nullptr;
+  const int64_t* bias = nullptr;
+  const int32_t* gather = nullptr;  // per-sample table [P][K]
+};
+
+}  // namespace
+}  // namespace pnb
+
+struct pnb_evaluator {
+  int device = 0;
+  pnb_params params{};
+  pnb::plan::Program prog;
+  std::vector<pnb_keys*> keys;  // per program level (null when unused)
+  pnb_keys* client = nullptr;   // the key set whose secret keys encrypt and decrypt
+  std::vector<pnb::DevInstr> dev;
+  std::vector<void*> allocations;
+  uint64_t* tvs = nullptr;  // [T][N]
+  // per-chunk resources
+  int chunk = 0;
+  std::vector<uint64_t*> bufs;
+  std::vector<int32_t*> gathers;  // per instruction: batch-expanded gather index
+  uint64_t* small = nullptr;
+  void* ks_ws = nullptr;
+  size_t ks_ws_bytes = 0;
+  int64_t max_pbs_rows = 0;
+  int chunk_limit = 1;  // samples per chunk allowed by the memory budget
+};
+
+namespace pnb {
+namespace {
+
+struct Guard {
+  int prev = -1;
+  int rc = PNB_OK;
+  explicit Guard(int dev) {
+    cudaError_t e = cudaGetDevice(&prev);
+    if (e != cudaSuccess) { rc = cuda_status(e, "cudaGetDevice"); return; }
+    if (prev != dev && (e = cudaSetDevice(dev)) != cudaSuccess) rc = cuda_status(e, "cudaSetDevice");
+  }
+  ~Guard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+void free_chunk(pnb_evaluator* ev) {
+  for (auto* p : ev->bufs) cudaFree(p);
+  for (auto* p : ev->gathers) cudaFree(p);
+  ev->bufs.clear();
+  ev->gathers.clear();
+  cudaFree(ev->small);
+  cudaFree(ev->ks_ws);
+  ev->small = nullptr;
+  ev->ks_ws = nullptr;
+  ev->chunk = 0;
+}
+
+int64_t row_words(const pnb_params& p) { return (int64_t)p.k * p.N + 1; }
+
+int alloc_chunk(pnb_evaluator* ev, int chunk) {
+  free_chunk(ev);
+  const int64_t L = row_words(ev->params);
+  const auto& P = ev->prog;
+  ev->bufs.assign(P.bufs.size(), nullptr);
+  for (size_t i = 0; i < P.bufs.size(); ++i)
+    PNB_CUDA(cudaMalloc((void**)&ev->bufs[i], (size_t)chunk * P.bufs[i].elems * L * 8));
+  ev->gathers.assign(P.code.size(), nullptr);
+  int64_t max_rows = 0;
+  for (size_t i = 0; i < P.code.size(); ++i) {
+    const auto& I = P.code[i];
+    if (I.kind == plan::Kind::Pbs)
+      max_rows = std::max<int64_t>(max_rows, (int64_t)chunk * P.bufs[I.dst].elems);
+    if (I.kind == plan::Kind::Contract && !I.gather.empty()) {
+      const int64_t n = (int64_t)chunk * I.P * I.K;
+      PNB_CUDA(cudaMalloc((void**)&ev->gathers[i], n * sizeof(int32_t)));
+      gather_batch_kernel<<<(unsigned)((n + 255) / 256), 256>>>(
+          ev->dev[i].gather, I.P, I.K, P.bufs[I.src].elems, chunk, ev->gathers[i]);
+      PNB_CHECK_LAUNCH("gather_batch_kernel");
+    }
+  }
+  ev->max_pbs_rows = std::min<int64_t>(max_rows, PBS_SLICE);
+  if (ev->max_pbs_rows > 0) {
+    const pnb_keys* K0 = ev->client;
+    PNB_CUDA(cudaMalloc((void**)&ev->small,
+                        (size_t)ev->max_pbs_rows * (K0->p.n + 1) * sizeof(uint64_t)));
+    ev->ks_ws_bytes = ks_tc_workspace_bytes(K0->p, (int)ev->max_pbs_rows);
+    PNB_CUDA(cudaMalloc(&ev->ks_ws, ev->ks_ws_bytes));
+  }
+  PNB_CUDA(cudaDeviceSynchronize());
+  ev->chunk = chunk;
+  return PNB_OK;
+}
+
+int run_lin(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batch,
+            cudaStream_t st) {
+  const auto& P = ev->prog;
+  LinArgs a;
+  memset(&a, 0, sizeof a);
+  a.dst = ev->bufs[I.dst];
+  a.E = P.bufs[I.dst].elems;
+  a.rows = (int64_t)batch * a.E;
+  a.L = (int)row_words(ev->params);
+  a.nt = (int)I.terms.size();
+  if (a.nt > LIN_TERMS) {
+    set_error("internal: linear combination with %d terms", a.nt);
+    return PNB_ERR_INVALID;
+  }
+  for (int t = 0; t < a.nt; ++t) {
+    const auto& T = I.terms[t];
+    a.src[t] = ev->bufs[T.src];
+    a.srcE[t] = P.bufs[T.src].elems;
+    a.coef[t] = D.coef[t];
+    a.coef_u[t] = T.coef.size() == 1 ? T.coef[0] : 0;
+    a.map[t] = D.map[t];
+  }
+  a.cst = D.cst;
+  a.cst_u = I.cst.size() == 1 ? I.cst[0] : 0;
+  if (a.rows == 0) return PNB_OK;
+  lin_kernel<<<(unsigned)((a.rows + 1) / 2), 256, 0, st>>>(a);
+  PNB_CHECK_LAUNCH("lin_kernel");
+  return PNB_OK;
+}
+
+int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batch,
+            cudaStream_t st) {
+  const auto& P = ev->prog;
+  const int64_t E = P.bufs[I.dst].elems;
+  const int64_t rows = (int64_t)batch * E;
+  const int L = (int)row_words(ev->params);
+  // stage the bootstrap input 2^shift * src + offset in the destination buffer
+  LinArgs a;
+  memset(&a, 0, sizeof a);
+  a.dst = ev->bufs[I.dst];
+  a.E = E;
+  a.rows = rows;
+  a.L = L;
+  a.nt = 1;
+  a.src[0] = ev->bufs[I.src];
+  a.srcE[0] = P.bufs[I.src].elems;
+  a.coef_u[0] = (int64_t)((uint64_t)1 << I.shift);
+  a.cst_u = I.offset;
+  if (rows == 0) return PNB_OK;
+  lin_kernel<<<(unsigned)((rows + 1) / 2), 256, 0, st>>>(a);
+  PNB_CHECK_LAUNCH("lin_kernel(bootstrap input)");
+  const pnb_keys* K = ev->keys[I.level];
+  const int64_t n1 = ev->client->p.n + 1;
+  for (int64_t r0 = 0; r0 < rows; r0 += ev->max_pbs_rows) {
+    const int cnt = (int)std::min<int64_t>(ev->max_pbs_rows, rows - r0);
+    uint64_t* x = ev->bufs[I.dst] + (size_t)r0 * L;
+    int rc = keyswitch_launch(ev->client, x, ev->small, cnt, ev->ks_ws, st);
+    if (rc) return rc;
+    // row r of the slice is element (r0 + r) % E of its sample
+    rc = blind_rotate_sel(K, ev->tvs, D.tv, (int)E, (int)(r0 % E), ev->small, x, cnt, st);
+    if (rc) return rc;
+  }
+  return PNB_OK;
+}
+
+int run_contract(pnb_evaluator* ev, size_t i, const plan::Instr& I, const DevInstr& D,
+                 int batch, cudaStream_t st) {
+  const int L = (int)row_words(ev->params);
+  if (I.gather.empty())
+    return lwe_contract_tc(D.W, D.bias, I.bias_delta, I.M, I.K, ev->bufs[I.src],
+                           ev->bufs[I.dst], batch, L, st);
+  return lwe_contract_gather_placed(D.W, D.bias, I.bias_delta, I.M, I.K, ev->bufs[I.src],
+                                    ev->gathers[i], batch * I.P, ev->bufs[I.dst], L, I.P, st);
+}
+
+}  // namespace
+}  // namespace pnb
+
+using namespace pnb;
+
+extern "C" {
+
+int pnb_graph_load(const char* json, size_t len, pnb_graph** out) {
+  if (!json || !out) {
+    set_error("pnb_graph_load: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  try {
+    pnb_graph* g = new pnb_graph;
+    try {
+      g->g = ir::parse_graph(json, len);
+      for (const auto& n : g->g.nodes) ir::validate_op(n.op);
+    } catch (...) {
+      delete g;
+      throw;
+    }
+    *out = g;
+    return PNB_OK;
+  } catch (const std::bad_alloc&) {
+    set_error("pnb_graph_load: out of host memory");
+    return PNB_ERR_OOM;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
+int pnb_graph_free(pnb_graph* g) {
+  delete g;
+  return PNB_OK;
+}
+
+int pnb_graph_info(const pnb_graph* g, int* num_nodes, int* num_blocks, int* input_bits) {
+  if (!g) {
+    set_error("pnb_graph_info: NULL graph");
+    return PNB_ERR_INVALID;
+  }
+  if (num_nodes) *num_nodes = (int)g->g.nodes.size();
+  if (num_blocks) *num_blocks = g->g.num_blocks;
+  if (input_bits) *input_bits = g->g.input_bits;
+  return PNB_OK;
+}
+
+int pnb_graph_check_budget(const pnb_graph* g) {
+  if (!g) {
+    set_error("pnb_graph_check_budget: NULL graph");
+    return PNB_ERR_INVALID;
+  }
+  try {
+    ir::check_graph_bit_width_budget(g->g);
+    return PNB_OK;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
+int pnb_plan_create(const pnb_graph* g, const pnb_params* p, const int64_t* input_lens,
+                    int64_t input_lo, int64_t input_hi, double margin_sigmas, pnb_plan** out) {
+  if (!g || !p || !out) {
+    set_error("pnb_plan_create: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  try {
+    plan::Options o;
+    o.input_lo = input_lo;
+    o.input_hi = input_hi;
+    if (margin_sigmas > 0) o.z = margin_sigmas;
+    o.n = p->n;
+    o.N = p->N;
+    o.log2_ksms = plan::ksms_log2_sigma(p->n, p->N, p->k, p->ks_base_log, p->ks_level, p->lwe_std);
+    o.log2_fresh = std::log2(p->glwe_std) + 64;
+    o.levels = plan::default_levels(p->n, p->N, p->k, p->glwe_std);
+    if (input_lens) o.input_lens.assign(input_lens, input_lens + g->g.inputs.size());
+    pnb_plan* pl = new pnb_plan;
+    try {
+      pl->prog = plan::build(g->g, o);
+    } catch (...) {
+      delete pl;
+      throw;
+    }
+    pl->params = *p;
+    *out = pl;
+    return PNB_OK;
+  } catch (const std::bad_alloc&) {
+    set_error("pnb_plan_create: out of host memory");
+    return PNB_ERR_OOM;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
+int pnb_plan_free(pnb_plan* p) {
+  delete p;
+  return PNB_OK;
+}
+
+int pnb_plan_info(const pnb_plan* p, pnb_plan_summary* info) {
+  if (!p || !info) {
+    set_error("pnb_plan_info: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  const auto& P = p->prog;
+  info->input_elems = P.input_elems;
+  info->output_elems = P.output_elems;
+  info->num_inputs = (int)P.inputs.size();
+  info->num_outputs = (int)P.outputs.size();
+  info->pbs_per_sample = P.pbs_per_sample;
+  info->cost_per_sample = P.cost_per_sample;
+  info->num_instructions = (int)P.code.size();
+  return PNB_OK;
+}
+
+int pnb_plan_tensor(const pnb_plan* p, int is_output, int idx, int64_t* elems, int* scale_log2,
+                    int64_t* lo, int64_t* hi) {
+  if (!p) {
+    set_error("pnb_plan_tensor: NULL plan");
+    return PNB_ERR_INVALID;
+  }
+  const auto& v = is_output ? p->prog.outputs : p->prog.inputs;
+  if (idx < 0 || idx >= (int)v.size()) {
+    set_error("pnb_plan_tensor: index %d out of range (%zu tensors)", idx, v.size());
+    return PNB_ERR_INVALID;
+  }
+  if (elems) *elems = v[idx].elems;
+  if (scale_log2) *scale_log2 = v[idx].scale;
+  if (lo) *lo = v[idx].lo;
+  if (hi) *hi = v[idx].hi;
+  return PNB_OK;
+}
+
+size_t pnb_plan_report(const pnb_plan* p, char* buf, size_t cap) {
+  if (!p) return 0;
+  const std::string& r = p->prog.report;
+  if (buf && cap > 0) {
+    const size_t n = std::min(cap - 1, r.size());
+    memcpy(buf, r.data(), n);
+    buf[n] = 0;
+  }
+  return r.size() + 1;
+}
+
+int pnb_plan_simulate(const pnb_plan* p, const int64_t* inputs, int batch, int64_t* outputs,
+                      double* min_margin) {
+  if (!p || !inputs || !outputs || batch < 0) {
+    set_error("pnb_plan_simulate: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  try {
+    plan::simulate(p->prog, inputs, batch, outputs, min_margin);
+    return PNB_OK;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
+int pnb_evaluator_free(pnb_evaluator* ev) {
+  if (!ev) return PNB_OK;
+  Guard g(ev->device);
+  free_chunk(ev);
+  for (void* a : ev->allocations) cudaFree(a);
+  cudaFree(ev->tvs);
+  for (pnb_keys* k : ev->keys)
+    if (k) pnb_keys_free(k);
+  delete ev;
+  return PNB_OK;
+}
+
+int pnb_evaluator_create(const pnb_plan* p, int device, uint64_t seed, size_t max_bytes,
+                         pnb_evaluator** out) {
+  if (!p || !out) {
+    set_error("pnb_evaluator_create: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  Guard guard(device);
+  if (guard.rc) return guard.rc;
+  pnb_evaluator* ev = new (std::nothrow) pnb_evaluator;
+  if (!ev) {
+    set_error("pnb_evaluator_create: out of host memory");
+    return PNB_ERR_OOM;
+  }
+  ev->device = device;
+  ev->params = p->params;
+  ev->prog = p->prog;
+  const auto& P = ev->prog;
+  int rc = PNB_OK;
+  // key sets: one per bootstrap level the program uses (same seed: same secret keys and KSK)
+  std::vector<char> used(P.levels.size(), 0);
+  for (const auto& I : P.code)
+    if (I.kind == plan::Kind::Pbs) used[I.level] = 1;
+  ev->keys.assign(P.levels.size(), nullptr);
+  for (size_t l = 0; l < P.levels.size() && rc == PNB_OK; ++l) {
+    if (!used[l] && !(l == 0 && ev->client == nullptr)) continue;
+    pnb_params q = p->params;
+    q.pbs_base_log = P.levels[l].base_log;
+    q.pbs_level = P.levels[l].level;
+    rc = pnb_keygen(device, &q, seed, &ev->keys[l]);
+    if (rc == PNB_OK && !ev->client) ev->client = ev->keys[l];
+  }
+  if (rc == PNB_OK && !ev->client) {
+    pnb_params q = p->params;
+    rc = pnb_keygen(device, &q, seed, &ev->keys[0]);
+    ev->client = ev->keys[0];
+  }
+  // test vectors
+  const int N = p->params.N;
+  if (rc == PNB_OK && !P.tvs.empty()) {
+    std::vector<uint64_t> t;
+    for (const auto& s : P.tvs) {
+      std::vector<uint64_t> m = plan::materialize_tv(s, N);
+      t.insert(t.end(), m.begin(), m.end());
+    }
+    rc = upload(t, &ev->tvs);
+  }
+  // per-instruction tables
+  ev->dev.assign(P.code.size(), DevInstr{});
+  auto keep = [&](void* a) {
+    if (a) ev->allocations.push_back(a);
+  };
+  for (size_t i = 0; i < P.code.size() && rc == PNB_OK; ++i) {
+    const auto& I = P.code[i];
+    DevInstr& D = ev->dev[i];
+    if (I.kind == plan::Kind::Lin) {
+      for (size_t t = 0; t < I.terms.size() && rc == PNB_OK; ++t) {
+        int64_t* c = nullptr;
+        int32_t* m = nullptr;
+        if (I.terms[t].coef.size() > 1) rc = upload(I.terms[t].coef, &c);
+        if (rc == PNB_OK) rc = upload(I.terms[t].map, &m);
+        keep(c);
+        keep(m);
+        D.coef[t] = c;
+        D.map[t] = m;
+      }
+      uint64_t* c = nullptr;
+      if (rc == PNB_OK && I.cst.size() > 1) rc = upload(I.cst, &c);
+      keep(c);
+      D.cst = c;
+    } else if (I.kind == plan::Kind::Pbs) {
+      int32_t* t = nullptr;
+      std::vector<int32_t> idx = I.tv;
+      if (idx.size() == 1) idx.assign((size_t)P.bufs[I.dst].elems, I.tv[0]);
+      rc = upload(idx, &t);
+      keep(t);
+      D.tv = t;
+    } else {
+      int8_t* w = nullptr;
+      int64_t* b = nullptr;
+      int32_t* gt = nullptr;
+      rc = upload(I.W, &w);
+      if (rc == PNB_OK) rc = upload(I.bias, &b);
+      if (rc == PNB_OK) rc = upload(I.gather, &gt);
+      keep(w);
+      keep(b);
+      keep(gt);
+      D.W = w;
+      D.bias = b;
+      D.gather = gt;
+    }
+  }
+  if (rc == PNB_OK) {
+    // chunk size: as many samples as fit the memory budget
+    int64_t per_sample = 0;
+    for (const auto& b : P.bufs) per_sample += b.elems * row_words(p->params) * 8;
+    size_t budget = max_bytes;
+    if (budget == 0) {
+      size_t fr = 0, tot = 0;
+      cudaMemGetInfo(&fr, &tot);
+      budget = fr / 2;
+    }
+    // the per-chunk buffers are allocated by the first evaluate (sized by its batch)
+    ev->chunk_limit = (int)std::max<int64_t>(
+        1, std::min<int64_t>(1 << 20, (int64_t)budget / std::max<int64_t>(per_sample, 1)));
+  }
+  if (rc != PNB_OK) {
+    pnb_evaluator_free(ev);
+    return rc;
+  }
+  *out = ev;
+  return PNB_OK;
+}
+
+int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys) {
+  if (!ev || !keys) {
+    set_error("pnb_evaluator_keys: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *keys = ev->client;
+  return PNB_OK;
+}
+
+int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t* out_dev,
+                 void* stream) {
+  if (!ev || batch < 0 || (batch > 0 && (!in_dev || !out_dev))) {
+    set_error("pnb_evaluate: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  if (batch == 0) return PNB_OK;
+  Guard guard(ev->device);
+  if (guard.rc) return guard.rc;
+  cudaStream_t st = (cudaStream_t)stream;
+  const auto& P = ev->prog;
+  const int64_t L = row_words(ev->params);
+  int rc = PNB_OK;
+  const int want = std::min(batch, ev->chunk_limit);
+  if (ev->chunk < want) rc = alloc_chunk(ev, want);
+  if (rc) return rc;
+  const int chunk = ev->chunk;
+  for (int b0 = 0; b0 < batch && rc == PNB_OK; b0 += chunk) {
+    const int nb = std::min(chunk, batch - b0);
+    int64_t off = 0;
+    for (const auto& io : P.inputs) {
+      cudaError_t e = cudaMemcpy2DAsync(
+          ev->bufs[io.buf], (size_t)io.elems * L * 8,
+          in_dev + ((size_t)b0 * P.input_elems + off) * L, (size_t)P.input_elems * L * 8,
+          (size_t)io.elems * L * 8, nb, cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_status(e, "pnb_evaluate: input copy");
+      off += io.elems;
+    }
+    for (size_t i = 0; i < P.code.size() && rc == PNB_OK; ++i) {
+      const auto& I = P.code[i];
+      switch (I.kind) {
+        case plan::Kind::Lin: rc = run_lin(ev, I, ev->dev[i], nb, st); break;
+        case plan::Kind::Pbs: rc = run_pbs(ev, I, ev->dev[i], nb, st); break;
+        case plan::Kind::Contract: rc = run_contract(ev, i, I, ev->dev[i], nb, st); break;
+      }
+    }
+    off = 0;
+    for (const auto& io : P.outputs) {
+      if (rc) break;
+      cudaError_t e = cudaMemcpy2DAsync(
+          out_dev + ((size_t)b0 * P.output_elems + off) * L, (size_t)P.output_elems * L * 8,
+          ev->bufs[io.buf], (size_t)io.elems * L * 8, (size_t)io.elems * L * 8, nb,
+          cudaMemcpyDeviceToDevice, st);
+      if (e != cudaSuccess) return cuda_status(e, "pnb_evaluate: output copy");
+      off += io.elems;
+    }
+  }
+  return rc;
+}
+
+}  // extern "C"

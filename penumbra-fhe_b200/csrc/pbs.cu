@@ -104,6 +104,19 @@ bool fft_tables_ready() {
 }
 
 // Coefficient t of X^r * P (negacyclic), r in [0, 2N).
+// Test-vector selection: ciphertext ct starts from tvs[idx[(first + ct) % period]]
+// (idx == nullptr: every ciphertext starts from tvs).
+struct TvSel {
+  const uint64_t* tvs;
+  const int32_t* idx;
+  int period;
+  int first;
+};
+__device__ __forceinline__ const uint64_t* tv_of(const TvSel& s, int ct) {
+  return s.idx ? s.tvs + (size_t)s.idx[(int)(((long long)s.first + ct) % s.period)] * FFT_N
+               : s.tvs;
+}
+
 __device__ __forceinline__ uint64_t rot_coef(const uint64_t* P, int t, int r) {
   int s = t - r;
   bool neg = false;
@@ -233,7 +246,7 @@ __device__ __forceinline__ void br_stage_ggsw(uint32_t dst, const double2* src, 
 
 template <int CPB>
 __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
-    const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
+    const uint64_t* __restrict__ small_ct, TvSel sel,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
     int base_log, FftTables tb) {
   using L = BrLayout<CPB>;
@@ -274,6 +287,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   if (threadIdx.x == 0) br_stage_ggsw(bsk_dst, fbsk, bar);
 
   const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
+  const uint64_t* tv = tv_of(sel, valid ? ct : 0);
   const int t64 = threadIdx.x & 63;
   for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
   const int bt = valid ? modswitch(in[n], LG) : 0;
@@ -400,7 +414,7 @@ __device__ __forceinline__ int64_t gadget_digit(uint64_t v, int beta, int lev) {
 
 template <int L>
 __global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
-    const uint64_t* __restrict__ small_ct, const uint64_t* __restrict__ tv,
+    const uint64_t* __restrict__ small_ct, TvSel sel,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
     int base_log, FftTables tb) {
   extern __shared__ __align__(16) unsigned char ml_raw[];
@@ -408,6 +422,7 @@ __global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ct = blockIdx.x;
   const uint64_t* in = small_ct + (size_t)ct * (n + 1);
+  const uint64_t* tv = tv_of(sel, ct);
   constexpr int LG = 12;
   for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
   const int bt = modswitch(in[n], LG);
@@ -482,7 +497,7 @@ __global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
 }
 
 template <int L>
-static int launch_ml(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
+static int launch_ml(const pnb_keys* K, TvSel tv, const uint64_t* small,
                      uint64_t* out, int count, FftTables tb, cudaStream_t st) {
   const int smem = sizeof(BrMlSmem);
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_ml_kernel<L>,
@@ -503,6 +518,16 @@ static bool br_supported(const pnb_params& p) {
 
 int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
                         uint64_t* out, int count, cudaStream_t st) {
+  return blind_rotate_sel(K, tv, nullptr, 1, 0, small, out, count, st);
+}
+
+int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_idx, int period,
+                     int first, const uint64_t* small, uint64_t* out, int count, cudaStream_t st) {
+  if (tv_idx && (period <= 0 || first < 0)) {
+    set_error("blind rotation: test-vector period must be positive");
+    return PNB_ERR_INVALID;
+  }
+  const TvSel tv{tvs, tv_idx, period, tv_idx ? first % period : 0};
   if (!br_supported(K->p)) {
     set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level 1..6, n<=%d (got "
               "k=%d N=%d level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
