@@ -1,5 +1,6 @@
 #!/usr/bin/env python3
-"""Benchmark of the batched programmable bootstrap (PBS/s) on B200.
+"""Benchmark of the batched programmable bootstrap (PBS/s) and of encrypted MLP inference
+(samples/s) on B200.
 
 Workload: the PBS microbenchmark -- a batch of 4096 LWE ciphertexts under
 n=834, k=1, N=2048, PBS gadget (2^23, 1), keyswitch gadget (2^3, 5), Gaussian noise at the
@@ -10,8 +11,14 @@ runtime/src/ops/activation.rs:115).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
 
+Second workload, reported under "mlp" in the same line: the 6-bit MLP 784-128-128-10 (graph
+quantized by the reference quantizer, tests/golden/cfg4_mlp.json) evaluated end to end under
+encryption -- the whole graph, every Linear on the tensor cores and every Requant as an exact
+bootstrap program -- on `--mlp-batch` synthetic samples per GPU (seeded uniform 6-bit inputs).
+
 N > 1 runs one process per GPU under torchrun; each rank bootstraps its own batch against
-its own key replica (weak scaling, no data-path collective), time = max over ranks.
+its own key replica (weak scaling, no data-path collective), time = max over ranks.  The MLP
+shards samples over ranks and reassembles the output ciphertexts with one NCCL all-gather.
 `--impl reference` times the CPU restatement of the same PBS (the oracle's f64 FFT path, the
 algorithm tfhe-rs runs on the CPU) on all host cores; it needs no GPU.
 """
@@ -160,6 +167,80 @@ def run_reference(args):
     return 0
 
 
+def mlp_leg(args, pnb, world, rank, local, dist, dev):
+    """Encrypted MLP inference over a sample shard per rank; returns the "mlp" object."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import ir_eval
+    with open(os.path.join(ROOT, "tests", "golden", "cfg4_mlp.json")) as f:
+        graph = json.load(f)["graph"]
+    plan = pnb.Plan(pnb.Graph(graph))
+    ev = pnb.Evaluator(plan, device=local, seed=SEED)  # identical keys on every rank
+    B = args.mlp_batch
+    rng = np.random.default_rng(SEED + 100 + rank)
+    x = rng.integers(0, 64, (B, plan.input_elems))
+    ct = ev.encrypt(x, seed=SEED + 7, first_index=rank * B * plan.input_elems)
+    ev.reserve(B)
+    ev.evaluate(ct[:1])  # warm-up
+    h_in = ct.cpu().pin_memory()
+    d_in = torch.empty_like(ct)
+    gathered = torch.empty((world * B, plan.output_elems, ct.shape[-1]), dtype=torch.int64,
+                           device=dev)
+    h_out = torch.empty(gathered.shape, dtype=torch.int64).pin_memory()
+    stream = torch.cuda.current_stream(dev)
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    evs[0].record(stream)
+    d_in.copy_(h_in, non_blocking=True)
+    evs[1].record(stream)
+    out = ev.evaluate(d_in)
+    evs[2].record(stream)
+    if dist is not None:
+        dist.all_gather_into_tensor(gathered, out)
+    else:
+        gathered.copy_(out)
+    evs[3].record(stream)
+    h_out.copy_(gathered, non_blocking=True)
+    evs[4].record(stream)
+    torch.cuda.synchronize(dev)
+    t_dev = evs[1].elapsed_time(evs[3])
+    t_e2e = evs[0].elapsed_time(evs[4])
+    t_gather = evs[2].elapsed_time(evs[3])
+    if dist is not None:
+        t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_dev, t_e2e = float(t[0]), float(t[1])
+    ok = None
+    if rank == 0:
+        # decrypt the gathered outputs of every rank's first samples and compare to the
+        # cleartext graph on the same integers
+        got = ev.decrypt(h_out.to(dev)).cpu().numpy()
+        ok = True
+        for r in range(world):
+            xr = np.random.default_rng(SEED + 100 + r).integers(0, 64, (B, plan.input_elems))
+            for i in range(min(B, 2)):
+                want = ir_eval.evaluate(graph, {"x": xr[i].tolist()})[graph["outputs"][0]]
+                ok = ok and got[r * B + i].tolist() == want
+    return {
+        "metric": "encrypted_mlp_samples_per_second", "value": world * B / (t_dev * 1e-3),
+        "unit": "samples/s", "samples_per_gpu": B, "global_batch": world * B,
+        "scaling": "weak", "ms": t_dev,
+        "config": {"workload": "MLP 784-128-128-10, ReLU fused in Requant, PTQ n_bits=6 "
+                               "(reference quantizer graph), 6-bit inputs",
+                   "parallelism": f"samples sharded over {world} GPU(s), outputs all-gathered "
+                                  "over NCCL"},
+        "bootstraps_per_sample": plan.pbs_per_sample,
+        "allgather_ms": t_gather,
+        "e2e": {"value": world * B / (t_e2e * 1e-3), "unit": "samples/s",
+                "h2d_bytes_per_step": int(h_in.numel() * 8),
+                "d2h_bytes_per_step": int(h_out.numel() * 8) if rank == 0 else 0},
+        "decrypt_ok": ok,
+    }
+
+
 def run_gpu(args):
     import numpy as np
     import torch
@@ -257,6 +338,8 @@ def run_gpu(args):
                 "kernel": "blind_rotate_kernel<4>",
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
+    mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, info = cpu_reference_run(args, args.ref_samples, 1, args.ref_steps)
@@ -283,6 +366,7 @@ def run_gpu(args):
             "gpu_launches": 3 * args.steps,
             "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
             "decrypt_ok": decrypt_ok and e2e_ok,
+            "mlp": mlp,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -300,6 +384,8 @@ def main():
     ap.add_argument("--ref-samples", type=int, default=1024)
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mlp-batch", type=int, default=32,
+                    help="encrypted MLP samples per GPU (0 skips the MLP leg)")
     args = ap.parse_args()
     if args.impl == "reference":
         return run_reference(args)

@@ -224,6 +224,9 @@ int pnb_plan_simulate(const pnb_plan* plan, const int64_t* inputs, int batch, in
 int pnb_evaluator_create(const pnb_plan* plan, int device, uint64_t seed, size_t max_bytes,
                          pnb_evaluator** out);
 int pnb_evaluator_free(pnb_evaluator* ev);
+/* Allocate the per-chunk buffers for batches of up to `batch` samples now (otherwise the first
+ * pnb_evaluate of a larger batch allocates them).  Blocking. */
+int pnb_evaluator_reserve(pnb_evaluator* ev, int batch);
 /* The evaluator's client key set (borrowed): encrypt inputs / decrypt outputs with it. */
 int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys);
 /* Evaluate `batch` samples: in_dev [batch][input_elems][kN+1], out_dev

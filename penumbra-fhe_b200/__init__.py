@@ -106,6 +106,7 @@ _SIGS = {
                                        C.POINTER(C.c_void_p)]),
     "pnb_evaluator_free": (C.c_int, [C.c_void_p]),
     "pnb_evaluator_keys": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
+    "pnb_evaluator_reserve": (C.c_int, [C.c_void_p, C.c_int]),
     "pnb_evaluate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
 }
 
@@ -542,6 +543,10 @@ class Evaluator:
         _check("pnb_evaluator_keys", lib().pnb_evaluator_keys(h, C.byref(k)))
         self.keys = KeySet(k, plan.params, device, seed, owner=self)
         self.row = plan.params.k * plan.params.N + 1
+
+    def reserve(self, batch: int):
+        """Allocate the ciphertext buffers for batches of up to ``batch`` samples now."""
+        _check("pnb_evaluator_reserve", lib().pnb_evaluator_reserve(self._h, batch))
 
     def encrypt(self, x, seed: int = 1, first_index: int = 0) -> torch.Tensor:
         """Encrypt integers [batch][input_elems] at each input tensor's scale."""

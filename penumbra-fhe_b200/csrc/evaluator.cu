@@ -569,6 +569,17 @@ int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys) {
   return PNB_OK;
 }
 
+int pnb_evaluator_reserve(pnb_evaluator* ev, int batch) {
+  if (!ev || batch < 0) {
+    set_error("pnb_evaluator_reserve: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  Guard guard(ev->device);
+  if (guard.rc) return guard.rc;
+  const int want = std::min(batch, ev->chunk_limit);
+  return ev->chunk < want ? alloc_chunk(ev, want) : PNB_OK;
+}
+
 int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t* out_dev,
                  void* stream) {
   if (!ev || batch < 0 || (batch > 0 && (!in_dev || !out_dev))) {

@@ -381,50 +381,54 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 constexpr int BR_CPB = 4;
 
 // ------------------------------------------------------------------------------------------
-// Blind rotation with pbs_level = L >= 2 (the low-noise bootstrap whose outputs feed another
-// contraction).  One block of 2 warps per ciphertext; warp p owns GLWE polynomial p.  The
-// accumulator keeps all 64 bits (L levels read up to L*base_log bits of it); for each level the
-// two warps transform their digit polynomials, exchange the spectra and accumulate their output
-// polynomial's spectrum in shared memory; one inverse FFT per warp closes the iteration.
-// ------------------------------------------------------------------------------------------
+// Multi-level blind rotation (pbs_level 2..6, the low-noise key sets).  One ciphertext per
+// 64-thread block, warp p owning accumulator polynomial p (u64 words: the gadget digits need
+// base_log * level > 32 bits of it).  Per CMux and level the warp forms its digit polynomial,
+// transforms it, exchanges the spectrum with the other warp in two 8 KB halves and accumulates
+// D_own * F[own row][p] + D_other * F[other row][p]; levels 0..L-2 accumulate in shared memory,
+// the last in registers, which then go through the inverse transform.  About 99 KB of shared
+// memory per block: two blocks (four warps) per SM.
 struct BrMlSmem {
-  uint64_t acc[2][FFT_N];
-  double2 facc[2][FFT_M];
-  double2 xbuf[2][FFT_M];
+  uint64_t acc[2][FFT_N];    // 32 KB accumulator (mask, body)
+  double2 facc[2][FFT_M];    // 32 KB spectrum partial sums over the first L-1 levels
+  double scratch[2][FFT_M];  // 16 KB transpose / exchange halves, one per warp
+  double2 wf[FFT_M];         // 16 KB forward twiddles
+  double2 twf[32], twi[32];
   uint16_t abar[BR_MAXN];
 };
 
-// Digit `lev` (0 = most significant) of the signed gadget decomposition of v.
+// Balanced base-2^beta digit `lev` (0 = most significant) of the top beta*L bits of v, rounded:
+// the balanced digits of st are the plain digits of st + sum_j 2^(beta-1) 2^(beta j), each
+// minus 2^(beta-1) (the top carry falls off mod 2^(beta L), as it does on the torus).
 template <int L>
-__device__ __forceinline__ int64_t gadget_digit(uint64_t v, int beta, int lev) {
+__device__ __forceinline__ int ml_digit(uint64_t v, int beta, int lev) {
   const int total = beta * L;
-  uint64_t st = (v >> (64 - total)) + ((v >> (63 - total)) & 1u);
-  const uint64_t mask = (1ull << beta) - 1, half = 1ull << (beta - 1);
-  int64_t d = 0;
-#pragma unroll
-  for (int j = L - 1; j >= 0; --j) {
-    const uint64_t x = st & mask;
-    st >>= beta;
-    const bool neg = x >= half;
-    if (j == lev) d = neg ? (int64_t)x - (int64_t)(1ull << beta) : (int64_t)x;
-    st += neg ? 1u : 0u;
-  }
-  return d;
+  const uint64_t st = (v >> (64 - total)) + ((v >> (63 - total)) & 1u);
+  const uint64_t half = 1ull << (beta - 1);
+  const uint64_t H = half * (((1ull << total) - 1) / ((1ull << beta) - 1));
+  const uint64_t u = (st + H) >> (beta * (L - 1 - lev));
+  return (int)(u & ((1ull << beta) - 1)) - (int)half;
 }
 
 template <int L>
-__global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
+__global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
     int base_log, FftTables tb) {
   extern __shared__ __align__(16) unsigned char ml_raw[];
   BrMlSmem& S = *reinterpret_cast<BrMlSmem*>(ml_raw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int p = warp;
   const int ct = blockIdx.x;
   const uint64_t* in = small_ct + (size_t)ct * (n + 1);
   const uint64_t* tv = tv_of(sel, ct);
   constexpr int LG = 12;
   for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
+  for (int e = threadIdx.x; e < FFT_M; e += 64) S.wf[e] = tb.wf[e];
+  if (threadIdx.x < 32) {
+    S.twf[threadIdx.x] = tb.twf[threadIdx.x];
+    S.twi[threadIdx.x] = tb.twi[threadIdx.x];
+  }
   const int bt = modswitch(in[n], LG);
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
   for (int t = threadIdx.x; t < FFT_N; t += 64) {
@@ -432,55 +436,58 @@ __global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
     S.acc[1][t] = rot_coef(tv, t, r0);
   }
   __syncthreads();
-  uint64_t* my = S.acc[warp];
-  double2* buf = S.xbuf[warp];
-  const double2* obuf = S.xbuf[warp ^ 1];
-  double2* facc = S.facc[warp];
-  constexpr int ROWS = 2 * L;
+  uint64_t* my = S.acc[p];
+  double* buf = S.scratch[p];
+  double2* xch = reinterpret_cast<double2*>(S.scratch[p]);
+  const double2* och = reinterpret_cast<const double2*>(S.scratch[p ^ 1]);
+  double2* facc = S.facc[p];
+  const double2* wi_g = tb.wi;
 
   for (int i = 0; i < n; ++i) {
     const int a = S.abar[i];
     if (a == 0) continue;  // X^0 - 1 = 0: the CMux leaves the accumulator unchanged
-    const double2* ggsw = fbsk + (size_t)i * ROWS * 2 * FFT_M;
+    const double2* ggsw = fbsk + (size_t)i * (2 * L) * 2 * FFT_M;
+    double2 x[FFT_R];
+#pragma unroll 1
     for (int lev = 0; lev < L; ++lev) {
-      double2 x[FFT_R];
 #pragma unroll
       for (int m = 0; m < 32; ++m) {
         if ((m & 7) == 0) asm volatile("" ::: "memory");
         const int j = lane + 32 * m;
         const uint64_t v0 = rot_coef(my, j, a) - my[j];
         const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
-        x[m] = make_double2((double)gadget_digit<L>(v0, base_log, lev),
-                            (double)gadget_digit<L>(v1, base_log, lev));
+        x[m] = make_double2((double)ml_digit<L>(v0, base_log, lev),
+                            (double)ml_digit<L>(v1, base_log, lev));
       }
-      fft_forward(x, buf, lane, tb);
+      fft_forward_h(x, buf, lane, S.wf, S.twf);
+      const double2* f_own = ggsw + ((size_t)(p * L + lev) * 2 + p) * FFT_M;
+      const double2* f_oth = ggsw + ((size_t)((p ^ 1) * L + lev) * 2 + p) * FFT_M;
+      const bool last = lev == L - 1;
 #pragma unroll
-      for (int r = 0; r < 32; ++r) buf[r * 32 + lane] = x[r];
-      __syncthreads();
-      // output polynomial `warp`: rows (warp, lev) and (other, lev) of the GGSW
-      const double2* f_own = ggsw + ((size_t)(warp * L + lev) * 2 + warp) * FFT_M;
-      const double2* f_oth = ggsw + ((size_t)((warp ^ 1) * L + lev) * 2 + warp) * FFT_M;
+      for (int h = 0; h < 2; ++h) {
 #pragma unroll
-      for (int r = 0; r < 32; ++r) {
-        if ((r & 7) == 0) asm volatile("" ::: "memory");
-        const int e = r * 32 + lane;
-        const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
-        const double2 dt = obuf[e];
-        const double2 p0 = cmul(x[r], fo);
-        double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
-                                 p0.y + fma(dt.x, ft.y, dt.y * ft.x));
-        if (lev > 0) {
-          const double2 o = facc[e];
-          v = make_double2(v.x + o.x, v.y + o.y);
+        for (int rr = 0; rr < 16; ++rr) xch[rr * 32 + lane] = x[16 * h + rr];
+        pair_sync(0);
+#pragma unroll
+        for (int rr = 0; rr < 16; ++rr) {
+          const int r = 16 * h + rr;
+          const int e = r * 32 + lane;
+          const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
+          const double2 dt = och[rr * 32 + lane];
+          const double2 p0 = cmul(x[r], fo);
+          double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
+                                   p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+          if (lev > 0) {
+            const double2 o = facc[e];
+            v = make_double2(v.x + o.x, v.y + o.y);
+          }
+          if (last) x[r] = v;
+          else facc[e] = v;
         }
-        facc[e] = v;
+        pair_sync(0);
       }
-      __syncthreads();
     }
-    double2 x[FFT_R];
-#pragma unroll
-    for (int r = 0; r < 32; ++r) x[r] = facc[r * 32 + lane];
-    fft_inverse(x, buf, lane, tb);
+    fft_inverse_h(x, buf, lane, wi_g, S.twi);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
@@ -488,8 +495,9 @@ __global__ void __launch_bounds__(64) blind_rotate_ml_kernel(
       my[j] += f64_to_torus(x[m].x);
       my[j + FFT_M] += f64_to_torus(x[m].y);
     }
-    __syncthreads();
+    __syncwarp();
   }
+  __syncthreads();
   uint64_t* o = out + (size_t)ct * (FFT_N + 1);
   for (int t = threadIdx.x; t < FFT_N; t += 64)
     o[t] = (t == 0) ? S.acc[0][0] : (uint64_t)0 - S.acc[0][FFT_N - t];

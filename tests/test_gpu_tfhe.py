@@ -166,7 +166,7 @@ def test_pbs_argument_errors(pnb, gkeys):
         pnb.test_vector(gkeys, list(range(3)))  # does not divide N
 
 
-@pytest.mark.parametrize("beta,level", [(15, 2), (7, 6)])
+@pytest.mark.parametrize("beta,level", [(15, 2), (11, 3), (10, 4), (7, 6)])
 def test_multilevel_bootstrap(pnb, oracle, beta, level):
     """Low-noise bootstrap (more gadget levels, same secret keys and keyswitching key)."""
     p = pnb.default_params()
@@ -190,4 +190,4 @@ def test_multilevel_bootstrap(pnb, oracle, beta, level):
     ratio = gpu_noise.var() / ref_noise.var()
     assert 0.5 < ratio < 2.0, f"noise variance ratio {ratio:.3f}"
     # the whole point of the extra levels: far below the one-level set's ~2^49
-    assert np.log2(gpu_noise.std()) < {2: 43.5, 6: 35.0}[level]
+    assert np.log2(gpu_noise.std()) < {2: 43.5, 3: 40.0, 4: 38.0, 6: 35.0}[level]
