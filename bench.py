@@ -16,6 +16,10 @@ quantized by the reference quantizer, tests/golden/cfg4_mlp.json) evaluated end 
 encryption -- the whole graph, every Linear on the tensor cores and every Requant as an exact
 bootstrap program -- on `--mlp-batch` synthetic samples per GPU (seeded uniform 6-bit inputs).
 
+Also in the line: "contraction" -- the encrypted Linear 784->128 (int4 weights, 256 samples of
+784 ciphertexts) on the tensor cores against the HBM roofline; "noise" -- the single-level
+bootstrap's output noise over ~1e5 bootstraps beside its analytic value.
+
 N > 1 runs one process per GPU under torchrun; each rank bootstraps its own batch against
 its own key replica (weak scaling, no data-path collective), time = max over ranks.  The MLP
 shards samples over ranks and reassembles the output ciphertexts with one NCCL all-gather.
@@ -44,6 +48,8 @@ WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussi
 # DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts, from the ncu
 # capture summarised in profiles/blind_rotate_pbs4096.md (None until that capture exists).
 BR_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes of one contract_tc_kernel launch of the contraction leg (None until captured).
+CONTRACT_TRAFFIC = None
 
 
 def load_package():
@@ -167,6 +173,99 @@ def run_reference(args):
     return 0
 
 
+def contraction_leg(args, pnb, local, dev, flush):
+    """Encrypted Linear 784 -> 128 (int4 weights, 256 samples) on the tensor cores.
+
+    HBM-bound: every input ciphertext is read once and every output written once, so the
+    roofline is algorithmic bytes / time against the measured copy bandwidth."""
+    import numpy as np
+    import torch
+    M, K, B = 128, 784, args.contract_batch
+    L = 2049
+    rng = np.random.default_rng(SEED + 3)
+    W = torch.tensor(rng.integers(-8, 8, (M, K)).astype(np.int8), device=dev)
+    bias = torch.tensor(rng.integers(-100, 100, M), device=dev)
+    X = torch.randint(-(1 << 62), 1 << 62, (B, K, L), dtype=torch.int64, device=dev)
+    Y = torch.empty((B, M, L), dtype=torch.int64, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 1)):
+        pnb.lwe_contract(W, bias, 1 << 40, X, out=Y)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(args.steps)]
+    torch.cuda.synchronize(dev)
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        pnb.lwe_contract(W, bias, 1 << 40, X, out=Y)
+        b.record(stream)
+    torch.cuda.synchronize(dev)
+    ms = [a.elapsed_time(b) for a, b in evs]
+    avg = sum(ms) / len(ms)
+    algo_bytes = B * K * L * 8 + B * M * L * 8 + M * K + M * 8
+    peak = _measured_hbm()
+    gbs = algo_bytes / (avg * 1e-3) / 1e9
+    macs = M * K * B * L
+    return {
+        "metric": "contraction_u64_macs_per_second", "value": macs / (avg * 1e-3),
+        "unit": "u64 MAC/s", "ms": avg,
+        "config": {"workload": f"Linear {K}->{M}, int4 weights U[-8,7], {B} samples of {K} "
+                               f"ciphertexts (kN+1 = {L} words)",
+                   "l2": "inputs (%.2f GB) exceed L2; flushed between steps" %
+                         (B * K * L * 8 / 1e9)},
+        "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak["value"], "unit": "GB/s",
+                     "frac": gbs / peak["value"], "peak_source": peak["source"],
+                     "kernel": "contract_tc_kernel", "algorithmic_bytes": algo_bytes,
+                     "traffic": CONTRACT_TRAFFIC},
+    }
+
+
+def _measured_hbm():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        for k in ("hbm_gbs", "hbm_GBps", "hbm"):
+            if k in d:
+                v = d[k]
+                v = v.get("value", v) if isinstance(v, dict) else v
+                return {"value": float(v), "source": "MEASURED_PEAKS.json " + k + " (of measured)"}
+    except Exception:
+        pass
+    return {"value": 6650.0, "source": "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"}
+
+
+def noise_leg(pnb, keys, dev, total=100352):
+    """Output noise of the single-level bootstrap over ~1e5 bootstraps (phase - LUT*delta)."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(SEED + 9)
+    B = 4096
+    lut = rng.integers(0, 16, 16)
+    tv = pnb.test_vector(keys, lut)
+    errs = []
+    n = 0
+    while n < total:
+        msgs = rng.integers(0, 16, B)
+        ct = pnb.encrypt(keys, torch.tensor(msgs), seed=SEED + 50 + n)
+        out = pnb.pbs_batch(keys, tv, ct)
+        ph = pnb.phase(keys, out).cpu().numpy()
+        want = (lut[msgs].astype(np.uint64) * np.uint64(keys.params.delta()))
+        errs.append((ph.view(np.uint64) - want).view(np.int64).astype(np.float64))
+        n += B
+    e = np.concatenate(errs)
+    # analytic variance of the same blind rotation (key noise through the digits + gadget
+    # rounding), for comparison
+    p = keys.params
+    s = p.glwe_std * 2.0 ** 64
+    Bb = 2.0 ** p.pbs_base_log
+    v1 = p.n * (p.k + 1) * p.pbs_level * p.N * (Bb * Bb / 12) * s * s
+    eps = 2.0 ** (64 - p.pbs_base_log * p.pbs_level)
+    v2 = (p.n / 2) * (1 + p.k * p.N / 2) * eps * eps / 12
+    return {"bootstraps": int(e.size), "log2_std": float(np.log2(e.std())),
+            "mean_over_std": float(e.mean() / e.std()),
+            "analytic_log2_std": float(0.5 * np.log2(v1 + v2)),
+            "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2))}
+
+
 def mlp_leg(args, pnb, world, rank, local, dist, dev):
     """Encrypted MLP inference over a sample shard per rank; returns the "mlp" object."""
     import numpy as np
@@ -199,7 +298,7 @@ def mlp_leg(args, pnb, world, rank, local, dist, dev):
     out = ev.evaluate(d_in)
     evs[2].record(stream)
     if dist is not None:
-        dist.all_gather_into_tensor(gathered, out)
+        gathered = pnb.gather_shards(out, world * B)  # rank r holds samples [r*B, (r+1)*B)
     else:
         gathered.copy_(out)
     evs[3].record(stream)
@@ -339,6 +438,9 @@ def run_gpu(args):
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
     mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
+    contraction = None if args.contract_batch <= 0 else contraction_leg(args, pnb, local, dev,
+                                                                           flush)
+    noise = noise_leg(pnb, keys, dev) if (rank == 0 and args.noise) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -367,6 +469,8 @@ def run_gpu(args):
             "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
             "decrypt_ok": decrypt_ok and e2e_ok,
             "mlp": mlp,
+            "contraction": contraction,
+            "noise": noise,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -384,6 +488,10 @@ def main():
     ap.add_argument("--ref-samples", type=int, default=1024)
     ap.add_argument("--ref-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--contract-batch", type=int, default=256,
+                    help="samples of the Linear 784->128 contraction leg (0 skips it)")
+    ap.add_argument("--noise", type=int, default=1,
+                    help="measure the bootstrap output noise over ~1e5 bootstraps (rank 0)")
     ap.add_argument("--mlp-batch", type=int, default=32,
                     help="encrypted MLP samples per GPU (0 skips the MLP leg)")
     args = ap.parse_args()

@@ -20,7 +20,8 @@ __all__ = [
     "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
-    "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator",
+    "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
+    "gather_shards", "evaluate_sharded",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -591,3 +592,45 @@ class Evaluator:
                 self._h = None
         except Exception:
             pass
+
+
+# ---- multi-GPU sharding ----------------------------------------------------------------------
+
+def shard(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """Samples [start, stop) of ``rank`` when ``batch`` samples are split over ``world`` ranks
+    (contiguous, sizes differing by at most one)."""
+    base, extra = divmod(batch, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+def gather_shards(local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
+    """All-gather per-rank shards (dim 0 = samples of ``shard(batch, world, rank)``) into the
+    full batch on every rank.  Shards are padded to the largest size for the collective (NCCL
+    on GPU tensors, gloo on CPU tensors) and trimmed afterwards."""
+    import torch.distributed as dist
+    world = dist.get_world_size(group)
+    sizes = [shard(batch, world, r) for r in range(world)]
+    cap = max(b - a for a, b in sizes)
+    buf = torch.zeros((cap,) + tuple(local.shape[1:]), dtype=local.dtype, device=local.device)
+    buf[:local.shape[0]] = local
+    out = torch.empty((world * cap,) + tuple(local.shape[1:]), dtype=local.dtype,
+                      device=local.device)
+    if local.is_cuda:
+        dist.all_gather_into_tensor(out, buf, group=group)
+    else:
+        dist.all_gather(list(out.chunk(world)), buf, group=group)
+    parts = [out[r * cap: r * cap + (b - a)] for r, (a, b) in enumerate(sizes)]
+    return torch.cat(parts)
+
+
+def evaluate_sharded(ev: "Evaluator", ct_all: torch.Tensor, group=None) -> torch.Tensor:
+    """Strong-scaled evaluation: every rank evaluates its contiguous shard of the batch
+    ``ct_all`` [batch][input_elems][kN+1] on its own GPU (identical key replicas from the same
+    seed), then one all-gather reassembles the output ciphertexts on every rank."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    a, b = shard(ct_all.shape[0], world, rank)
+    local = ev.evaluate(ct_all[a:b].contiguous()) if b > a else torch.empty(
+        (0, ev.plan.output_elems, ev.row), dtype=torch.int64, device=ct_all.device)
+    return gather_shards(local, ct_all.shape[0], group)

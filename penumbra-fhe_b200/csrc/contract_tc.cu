@@ -122,15 +122,18 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
 
   if (warp < 4) {
     // ---------------- gather producers: 4 warps x 32 columns, 32 rows each per stage ---------
-    int kb_global = 0;
-    int pending_stage = -1;
+    // Copies of up to CT_LAG stages stay in flight; stage kb_global - CT_LAG is released (its
+    // mbarrier arrive) once its group has landed.  CT_LAG <= CT_STAGES - 1 keeps the ring live:
+    // refilling stage s waits for the MMAs of its previous use, released CT_LAG groups earlier.
+    constexpr int CT_LAG = CT_STAGES - 1;
+    int kb_global = 0, released = 0;
     for (int t = blockIdx.x; t < total && !*abort_s; t += gridDim.x) {
       const int nt = t % a.n_tiles;
       const int mt = (t / a.n_tiles) % a.m_tiles;
       const int g = t / (a.n_tiles * a.m_tiles);
       const int col = nt * 32 + lane;
       const bool col_ok = col < a.L;
-      const int32_t* idx_g = a.idx + (size_t)g * a.K;
+      const int32_t* idx_g = a.idx ? a.idx + (size_t)g * a.K : nullptr;
       for (int kb = 0; kb < a.k_blocks; ++kb, ++kb_global) {
         const int s = kb_global % CT_STAGES;
         const uint32_t use = (uint32_t)(kb_global / CT_STAGES);
@@ -143,7 +146,8 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
         }
         // this lane's row index for the 32 rows of the warp: k = kb*128 + warp + 4*i
         const int kr = kb * CT_BK + warp + 4 * lane;
-        const int my_idx = (kr < a.K) ? __ldg(idx_g + kr) : -1;
+        // dense operand (idx == null): ciphertext g*K + k
+        const int my_idx = (kr >= a.K) ? -1 : idx_g ? __ldg(idx_g + kr) : g * a.K + kr;
         const int box = lane >> 4, ch = (lane & 15) >> 1, half = lane & 1;
 #pragma unroll 4
         for (int i = 0; i < 32; ++i) {
@@ -156,20 +160,17 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
           cp_async8(dst, src, ok ? 8u : 0u);
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
-        // release the previous stage once its copies have landed
-        if (pending_stage >= 0) {
-          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        if (kb_global + 1 - released > CT_LAG) {
+          asm volatile("cp.async.wait_group %0;" ::"n"(CT_LAG) : "memory");
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-          tc::mbar_arrive(full(pending_stage));
+          tc::mbar_arrive(full(released % CT_STAGES));
+          ++released;
         }
-        pending_stage = s;
       }
     }
-    if (pending_stage >= 0) {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      tc::mbar_arrive(full(pending_stage));
-    }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    for (; released < kb_global; ++released) tc::mbar_arrive(full(released % CT_STAGES));
   } else if (warp == 4) {
     // ---------------- MMA issue (one elected lane) --------------------------------------------
     if (lane == 0) {
@@ -255,10 +256,6 @@ __global__ void pad_weights_kernel(const int8_t* __restrict__ W, int M, int K, i
 }
 
 // idx[g][k] = g*K + k: the dense (Linear) gather.
-__global__ void dense_index_kernel(int32_t* idx, int G, int K) {
-  const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i < (size_t)G * K) idx[i] = (int32_t)i;
-}
 
 static int sm_count() {
   int dev = 0, n = 0;
@@ -333,17 +330,13 @@ int lwe_contract_gather_placed(const int8_t* W, const int64_t* bias, uint64_t de
 int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                     const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st) {
   if (batch <= 0) return batch == 0 ? PNB_OK : PNB_ERR_INVALID;
-  int32_t* idx = nullptr;
-  PNB_CUDA(cudaMallocAsync((void**)&idx, sizeof(int32_t) * (size_t)batch * K, st));
-  const size_t n = (size_t)batch * K;
-  dense_index_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(idx, batch, K);
-  int rc = PNB_OK;
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) rc = cuda_status(e, "dense_index_kernel");
-  if (rc == PNB_OK) rc = lwe_contract_gather(W, bias, delta, M, K, X, idx, batch, Y, L, st);
-  e = cudaFreeAsync(idx, st);
-  if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(index)");
-  return rc;
+  if ((long long)batch * K > 0x7fffffffLL) {
+    set_error("contract: batch * K = %lld exceeds the 32-bit ciphertext index",
+              (long long)batch * K);
+    return PNB_ERR_INVALID;
+  }
+  // a null index makes the gather dense: group g reads ciphertexts g*K .. g*K + K-1
+  return lwe_contract_gather_placed(W, bias, delta, M, K, X, nullptr, batch, Y, L, 0, st);
 }
 
 }  // namespace pnb

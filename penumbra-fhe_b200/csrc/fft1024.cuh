@@ -177,6 +177,37 @@ __device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, 
   for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], twi_s[n]);
 }
 
+// Forward twiddle table held once in shared memory for both directions.  Element (a, b) of the
+// 32x32 table lives at a*32 + ((a+b) & 31): the forward FFT reads row r across the lanes and the
+// inverse reads the transpose (its twiddle (n, lane) is the conjugate of forward element
+// (lane, n)); with this swizzle both patterns are bank-conflict free.
+__device__ __forceinline__ int tw_swz(int a, int b) { return a * 32 + ((a + b) & 31); }
+
+__device__ __forceinline__ void fft_forward_s(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wf_sw, const double2* twf_s) {
+#pragma unroll
+  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], twf_s[m]);
+  dft32_dif(x);
+#pragma unroll
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], wf_sw[tw_swz(r, lane)]);
+  warp_transpose_half(x, buf, lane);
+  dft32_dif(x);
+}
+
+__device__ __forceinline__ void fft_inverse_s(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wf_sw, const double2* twi_s) {
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) {
+    const double2 w = wf_sw[tw_swz(lane, n)];  // inverse twiddle = conj(w)
+    x[n] = make_double2(fma(x[n].x, w.x, x[n].y * w.y), fma(x[n].x, -w.y, x[n].y * w.x));
+  }
+  warp_transpose_half(x, buf, lane);
+  idft32_dit(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], twi_s[n]);
+}
+
 // Forward negacyclic FFT of one folded polynomial (see header comment).
 __device__ __forceinline__ void fft_forward(double2 (&x)[FFT_R], double2* buf, int lane,
                                             const FftTables& tb) {

@@ -204,13 +204,12 @@ struct BrLayout {
   static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);           // 2 KB per ciphertext
   static constexpr int OFF_ACC = WARPS * SCRATCH;
   static constexpr int OFF_BSK = OFF_ACC + WARPS * ACC;
-  static constexpr int OFF_WF = OFF_BSK + BSK;                      // 16 KB forward twiddles
+  static constexpr int OFF_WF = OFF_BSK + BSK;  // 16 KB twiddles (both directions, swizzled)
   static constexpr int OFF_TWF = OFF_WF + FFT_M * (int)sizeof(double2);
   static constexpr int OFF_TWI = OFF_TWF + 32 * (int)sizeof(double2);
   static constexpr int OFF_ABAR = OFF_TWI + 32 * (int)sizeof(double2);
   static constexpr int OFF_BAR = OFF_ABAR + CPB * ABAR;
-  static constexpr int OFF_TAB = OFF_BAR + 16;
-  static constexpr int BYTES = OFF_TAB + 16;
+  static constexpr int BYTES = OFF_BAR + 16;
 };
 
 // The blind rotation's inverse FFT leaves v * 2^-32, v the integer nearest the exact product
@@ -269,15 +268,13 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   const uint32_t bar = tc::smem_u32(br_raw + L::OFF_BAR);
   volatile int* abort_s = reinterpret_cast<volatile int*>(br_raw + L::OFF_BAR + 8);
   const uint32_t bsk_dst = tc::smem_u32(br_raw + L::OFF_BSK);
-  const double2* volatile* wi_s = reinterpret_cast<const double2* volatile*>(br_raw + L::OFF_TAB);
 
   if (threadIdx.x == 0) {
     tc::mbar_init(bar, 1);
     tc::fence_mbar_init();
     *abort_s = 0;
-    *wi_s = tb.wi;
   }
-  for (int e = threadIdx.x; e < FFT_M; e += 64 * CPB) wf_s[e] = tb.wf[e];
+  for (int e = threadIdx.x; e < FFT_M; e += 64 * CPB) wf_s[tw_swz(e >> 5, e & 31)] = tb.wf[e];
   if (threadIdx.x < 32) {
     twf_s[threadIdx.x] = tb.twf[threadIdx.x];
     const double2 t = tb.twi[threadIdx.x];
@@ -302,7 +299,6 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   const double2* f_oth = bsk_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
 
   for (int i = 0; i < n; ++i) {
-    const double2* wi_g = *wi_s;  // re-read so the inverse-twiddle loads stay inside the loop
     const int a = abar[i];
     // X^a = (-1)^(a >= N) X^(a mod N): rotate by ar in [0, N), flip the sign where it wraps.
     const int ar = a & (FFT_N - 1);
@@ -322,7 +318,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
       const int d1 = (int)(v1 + rnd) >> shift;
       x[m] = make_double2((double)d0, (double)d1);
     }
-    fft_forward_h(x, buf, lane, wf_s, twf_s);
+    fft_forward_s(x, buf, lane, wf_s, twf_s);
     // GGSW i must have landed in shared memory (bounded wait; parity = i mod 2).
     if (!tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT)) {
       *abort_s = 1;
@@ -354,7 +350,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
     }
-    fft_inverse_h(x, buf, lane, wi_g, twi_s);
+    fft_inverse_s(x, buf, lane, wf_s, twi_s);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
@@ -446,6 +442,7 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
   for (int i = 0; i < n; ++i) {
     const int a = S.abar[i];
     if (a == 0) continue;  // X^0 - 1 = 0: the CMux leaves the accumulator unchanged
+
     const double2* ggsw = fbsk + (size_t)i * (2 * L) * 2 * FFT_M;
     double2 x[FFT_R];
 #pragma unroll 1
