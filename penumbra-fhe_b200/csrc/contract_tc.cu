@@ -50,9 +50,22 @@ constexpr int CT_STAGES = 4;
 constexpr int CT_A_BYTES = CT_BM * CT_BK;    // 16 KB
 constexpr int CT_B_BYTES = CT_BK * CT_BN;    // 32 KB
 constexpr int CT_STAGE_BYTES = CT_A_BYTES + CT_B_BYTES;
-constexpr int CT_PRODUCERS = 128;            // gathering threads (warps 0..3)
-constexpr int CT_THREADS = 288;              // + MMA warp (4) + epilogue warps (5..8)
-constexpr int CT_SMEM = CT_STAGES * CT_STAGE_BYTES + 1024 + 256;
+#ifndef CT_PROD_WARPS
+#define CT_PROD_WARPS 8
+#endif
+constexpr int CT_PW = CT_PROD_WARPS;          // gathering warps 0..CT_PW-1
+constexpr int CT_PRODUCERS = 32 * CT_PW;
+constexpr int CT_ROWS_PER_WARP = CT_BK / CT_PW;
+constexpr int CT_MMA_WARP = CT_PW;
+#ifndef CT_EPI_WARP_COUNT
+#define CT_EPI_WARP_COUNT 4
+#endif
+constexpr int CT_EPI_WARPS = CT_EPI_WARP_COUNT;      // 4 or 8: one or two per TMEM lane quarter
+constexpr int CT_EPI_WORDS = 32 * 4 / CT_EPI_WARPS;  // output words per epilogue warp (32 / 16)
+constexpr int CT_EPI_CPAIRS = CT_EPI_WORDS / 8;      // chunk pairs (2 x 4 words) per warp
+constexpr int CT_THREADS = 32 * (CT_PW + 1 + CT_EPI_WARPS);
+constexpr int CT_EPI_BYTES = CT_EPI_WARPS * 32 * CT_EPI_WORDS * 8;  // per warp: 32 rows
+constexpr int CT_SMEM = CT_STAGES * CT_STAGE_BYTES + 1024 + 256 + CT_EPI_BYTES;
 constexpr uint32_t CT_IDESC = tc::idesc_i8(CT_BM, CT_BN, /*a_signed=*/true,
                                            /*b_signed=*/false, /*a_mn=*/false, /*b_mn=*/true);
 constexpr uint32_t CT_WAIT_LIMIT = 1u << 24;
@@ -106,13 +119,13 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
     }
     for (int b = 0; b < 2; ++b) {
       tc::mbar_init(acc_full(b), 1);
-      tc::mbar_init(acc_empty(b), 128);
+      tc::mbar_init(acc_empty(b), 32 * CT_EPI_WARPS);
     }
     *abort_s = 0;
     tc::fence_mbar_init();
     tc::prefetch_tmap(&tmW);
   }
-  if (warp == 4) tc::tmem_alloc(holder, 512);
+  if (warp == CT_MMA_WARP) tc::tmem_alloc(holder, 512);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
@@ -120,8 +133,8 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
 
   const int total = a.G * a.m_tiles * a.n_tiles;
 
-  if (warp < 4) {
-    // ---------------- gather producers: 4 warps x 32 columns, 32 rows each per stage ---------
+  if (warp < CT_PW) {
+    // ---------------- gather producers: CT_PW warps x 32 columns, CT_BK/CT_PW rows each -------
     // Copies of up to CT_LAG stages stay in flight; stage kb_global - CT_LAG is released (its
     // mbarrier arrive) once its group has landed.  CT_LAG <= CT_STAGES - 1 keeps the ring live:
     // refilling stage s waits for the MMAs of its previous use, released CT_LAG groups earlier.
@@ -144,14 +157,14 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
           tc::mbar_expect_tx(full(s), CT_A_BYTES);
           tc::tma_load_2d(a_s, &tmW, kb * CT_BK, mt * CT_BM, full(s));
         }
-        // this lane's row index for the 32 rows of the warp: k = kb*128 + warp + 4*i
-        const int kr = kb * CT_BK + warp + 4 * lane;
+        // lane i < CT_ROWS_PER_WARP holds the index of row k = kb*CT_BK + warp + CT_PW*i
+        const int kr = kb * CT_BK + warp + CT_PW * lane;
         // dense operand (idx == null): ciphertext g*K + k
         const int my_idx = (kr >= a.K) ? -1 : idx_g ? __ldg(idx_g + kr) : g * a.K + kr;
         const int box = lane >> 4, ch = (lane & 15) >> 1, half = lane & 1;
 #pragma unroll 4
-        for (int i = 0; i < 32; ++i) {
-          const int r = warp + 4 * i;  // row within the stage
+        for (int i = 0; i < CT_ROWS_PER_WARP; ++i) {
+          const int r = warp + CT_PW * i;  // row within the stage
           const int x = __shfl_sync(0xffffffffu, my_idx, i);
           const bool ok = col_ok && x >= 0;
           const uint64_t* src = ok ? a.X + (size_t)x * a.L + col : a.X;
@@ -171,7 +184,7 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     for (; released < kb_global; ++released) tc::mbar_arrive(full(released % CT_STAGES));
-  } else if (warp == 4) {
+  } else if (warp == CT_MMA_WARP) {
     // ---------------- MMA issue (one elected lane) --------------------------------------------
     if (lane == 0) {
       int kb_global = 0, tt = 0;
@@ -202,8 +215,17 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
       }
     }
   } else {
-    // ---------------- epilogue: warps 5..8 -> TMEM lane quarters 1, 2, 3, 0 -----------------
-    const int q = warp & 3;
+    // ---------------- epilogue: the last 8 warps ----------------------------------------------
+    // Warp w reads TMEM lane quarter w % 4 (its 32 output rows) and half e / 4 (e = epilogue
+    // warp number) of the
+    // tile's 32 output words: chunks of 32 columns = 4 words of 8 byte-limbs each.  The limbs
+    // are recombined into u64 words, staged in shared memory (XOR-swizzled rows of 16 words)
+    // after the TMEM buffer is released, and written out as 128-byte row segments.
+    const int e_w = warp - CT_MMA_WARP - 1;
+    const int q = warp & 3, eh = e_w >> 2;
+    constexpr int EW = CT_EPI_WORDS;
+    uint64_t* stage = reinterpret_cast<uint64_t*>(ct_raw + (bars + 256 - raw)) +
+                      (size_t)e_w * 32 * EW;
     int tt = 0;
     for (int t = blockIdx.x; t < total && !*abort_s; t += gridDim.x, ++tt) {
       const int nt = t % a.n_tiles;
@@ -212,35 +234,51 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
       const int buf = tt & 1;
       if (!ct_wait(acc_full(buf), (uint32_t)(tt >> 1) & 1u, abort_s)) break;
       tc::tc_fence_after();
-      const int row = mt * CT_BM + q * 32 + lane;
-      const bool row_ok = row < a.M;
-      const uint64_t bterm = (row_ok && a.bias) ? (uint64_t)a.bias[row] * a.delta : 0;
-      const int r_ = row_ok ? row : 0;
-      const size_t yr = a.P > 0 ? ((size_t)(g / a.P) * a.M + r_) * a.P + (g % a.P)
-                                : (size_t)g * a.M + r_;
-      uint64_t* yrow = a.Y + yr * a.L;
+      const uint32_t tbase = tmem + (uint32_t)(buf * 256) + ((uint32_t)(q * 32) << 16) +
+                             (uint32_t)(eh * (EW / 4) * 32);
 #pragma unroll 1
-      for (int chunk = 0; chunk < CT_BN / 32; ++chunk) {
-        uint32_t r[32];
-        tc::tmem_ld_32x32(tmem + (uint32_t)(buf * 256) + ((uint32_t)(q * 32) << 16) +
-                              (uint32_t)(chunk * 32),
-                          r);
+      for (int cp = 0; cp < CT_EPI_CPAIRS; ++cp) {
+        uint32_t r0[32], r1[32];
+        tc::tmem_ld_32x32_nowait(tbase + (uint32_t)(cp * 64), r0);
+        tc::tmem_ld_32x32_nowait(tbase + (uint32_t)(cp * 64 + 32), r1);
+        tc::tmem_ld_wait();
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < 8; ++u) {
           uint64_t v = 0;
 #pragma unroll
-          for (int b = 0; b < 8; ++b) v += (uint64_t)(int64_t)(int32_t)r[u * 8 + b] << (8 * b);
-          const int col = nt * 32 + chunk * 4 + u;
-          if (row_ok && col < a.L) yrow[col] = v + (col == a.L - 1 ? bterm : 0);
+          for (int b = 0; b < 8; ++b) {
+            const uint32_t c = u < 4 ? r0[u * 8 + b] : r1[(u - 4) * 8 + b];
+            v += (uint64_t)(int64_t)(int32_t)c << (8 * b);
+          }
+          const int w = cp * 8 + u;  // word within this warp's EW
+          stage[lane * EW + (w ^ (lane & (EW - 1)))] = v;
         }
       }
       tc::tc_fence_before();
       tc::mbar_arrive(acc_empty(buf));
+      __syncwarp();
+      // 32/EW rows per instruction, EW lanes x 8 bytes = one contiguous row segment each
+      constexpr int RPI = 32 / EW;
+      const int w = lane & (EW - 1);
+      const int col = nt * 32 + eh * EW + w;
+#pragma unroll 4
+      for (int i = 0; i < 32 / RPI; ++i) {
+        const int rr = RPI * i + lane / EW;
+        const int row = mt * CT_BM + q * 32 + rr;
+        uint64_t v = stage[rr * EW + (w ^ (rr & (EW - 1)))];
+        if (row < a.M && col < a.L) {
+          if (col == a.L - 1 && a.bias) v += (uint64_t)a.bias[row] * a.delta;
+          const size_t yr = a.P > 0 ? ((size_t)(g / a.P) * a.M + row) * a.P + (g % a.P)
+                                    : (size_t)g * a.M + row;
+          a.Y[yr * a.L + col] = v;
+        }
+      }
+      __syncwarp();
     }
   }
   tc::tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == CT_MMA_WARP) {
     tc::tc_fence_after();
     tc::tmem_dealloc(tmem, 512);
   }

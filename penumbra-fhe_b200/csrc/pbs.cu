@@ -395,18 +395,30 @@ struct BrMlSmem {
 
 // Balanced base-2^beta digit `lev` (0 = most significant) of the top beta*L bits of v, rounded:
 // the balanced digits of st are the plain digits of st + sum_j 2^(beta-1) 2^(beta j), each
-// minus 2^(beta-1) (the top carry falls off mod 2^(beta L), as it does on the torus).
-template <int L>
-__device__ __forceinline__ int ml_digit(uint64_t v, int beta, int lev) {
+// minus 2^(beta-1) (the top carry falls off mod 2^(beta L), as it does on the torus).  BETA > 0
+// makes every constant a compile-time value; BETA = 0 takes beta at run time.
+template <int L, int BETA>
+__device__ __forceinline__ int ml_digit(uint64_t v, int beta_rt, int lev) {
+  const int beta = BETA > 0 ? BETA : beta_rt;
   const int total = beta * L;
   const uint64_t st = (v >> (64 - total)) + ((v >> (63 - total)) & 1u);
   const uint64_t half = 1ull << (beta - 1);
-  const uint64_t H = half * (((1ull << total) - 1) / ((1ull << beta) - 1));
+  uint64_t H = 0;
+#pragma unroll
+  for (int j = 0; j < L; ++j) H |= half << (beta * j);
   const uint64_t u = (st + H) >> (beta * (L - 1 - lev));
   return (int)(u & ((1ull << beta) - 1)) - (int)half;
 }
 
-template <int L>
+// Streaming read of the bootstrapping key: no L1 allocation, so the key stream (32 KB per
+// warp and level) does not evict the lines that hold the kernel's register spills.
+__device__ __forceinline__ double2 ld_key_stream(const double2* p) {
+  double2 v;
+  asm("ld.global.nc.L1::no_allocate.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
+  return v;
+}
+
+template <int L, int BETA>
 __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
@@ -432,11 +444,11 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     S.acc[1][t] = rot_coef(tv, t, r0);
   }
   __syncthreads();
-  uint64_t* my = S.acc[p];
-  double* buf = S.scratch[p];
-  double2* xch = reinterpret_cast<double2*>(S.scratch[p]);
-  const double2* och = reinterpret_cast<const double2*>(S.scratch[p ^ 1]);
-  double2* facc = S.facc[p];
+  uint64_t* my0 = S.acc[p];
+  double* buf0 = S.scratch[p];
+  double2* xch0 = reinterpret_cast<double2*>(S.scratch[p]);
+  const double2* och0 = reinterpret_cast<const double2*>(S.scratch[p ^ 1]);
+  double2* facc0 = S.facc[p];
   const double2* wi_g = tb.wi;
 
   for (int i = 0; i < n; ++i) {
@@ -447,14 +459,23 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     double2 x[FFT_R];
 #pragma unroll 1
     for (int lev = 0; lev < L; ++lev) {
+      // Opaque per-level copies of the shared-memory pointers (three levels and more): every
+      // address below is loop invariant, and hoisting all of them out of the level loop spills
+      // registers.
+      uint64_t* my = my0;
+      double* buf = buf0;
+      double2* xch = xch0;
+      const double2* och = och0;
+      double2* facc = facc0;
+      if (L > 2) asm volatile("" : "+l"(my), "+l"(buf), "+l"(xch), "+l"(och), "+l"(facc));
 #pragma unroll
       for (int m = 0; m < 32; ++m) {
         if ((m & 7) == 0) asm volatile("" ::: "memory");
         const int j = lane + 32 * m;
         const uint64_t v0 = rot_coef(my, j, a) - my[j];
         const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
-        x[m] = make_double2((double)ml_digit<L>(v0, base_log, lev),
-                            (double)ml_digit<L>(v1, base_log, lev));
+        x[m] = make_double2((double)ml_digit<L, BETA>(v0, base_log, lev),
+                            (double)ml_digit<L, BETA>(v1, base_log, lev));
       }
       fft_forward_h(x, buf, lane, S.wf, S.twf);
       const double2* f_own = ggsw + ((size_t)(p * L + lev) * 2 + p) * FFT_M;
@@ -469,7 +490,7 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
         for (int rr = 0; rr < 16; ++rr) {
           const int r = 16 * h + rr;
           const int e = r * 32 + lane;
-          const double2 fo = __ldg(&f_own[e]), ft = __ldg(&f_oth[e]);
+          const double2 fo = ld_key_stream(&f_own[e]), ft = ld_key_stream(&f_oth[e]);
           const double2 dt = och[rr * 32 + lane];
           const double2 p0 = cmul(x[r], fo);
           double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
@@ -484,13 +505,13 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
         pair_sync(0);
       }
     }
-    fft_inverse_h(x, buf, lane, wi_g, S.twi);
+    fft_inverse_h(x, buf0, lane, wi_g, S.twi);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      my[j] += f64_to_torus(x[m].x);
-      my[j + FFT_M] += f64_to_torus(x[m].y);
+      my0[j] += f64_to_torus(x[m].x);
+      my0[j + FFT_M] += f64_to_torus(x[m].y);
     }
     __syncwarp();
   }
@@ -501,16 +522,25 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
   if (threadIdx.x == 0) o[FFT_N] = S.acc[1][0];
 }
 
-template <int L>
+template <int L, int BETA>
 static int launch_ml(const pnb_keys* K, TvSel tv, const uint64_t* small,
                      uint64_t* out, int count, FftTables tb, cudaStream_t st) {
   const int smem = sizeof(BrMlSmem);
-  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_ml_kernel<L>,
+  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_ml_kernel<L, BETA>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blind_rotate_ml_kernel<L><<<count, 64, smem, st>>>(small, tv, K->fbsk, out, count, K->p.n,
-                                                     K->p.pbs_base_log, tb);
+  blind_rotate_ml_kernel<L, BETA><<<count, 64, smem, st>>>(small, tv, K->fbsk, out, count,
+                                                           K->p.n, K->p.pbs_base_log, tb);
   PNB_CHECK_LAUNCH("blind_rotate_ml_kernel");
   return PNB_OK;
+}
+
+// The key sets the graph planner uses get kernels with compile-time gadget constants.
+template <int L, int B0, int B1 = 0>
+static int launch_ml_any(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64_t* out,
+                         int count, FftTables tb, cudaStream_t st) {
+  if (B0 > 0 && K->p.pbs_base_log == B0) return launch_ml<L, B0>(K, tv, small, out, count, tb, st);
+  if (B1 > 0 && K->p.pbs_base_log == B1) return launch_ml<L, B1>(K, tv, small, out, count, tb, st);
+  return launch_ml<L, 0>(K, tv, small, out, count, tb, st);
 }
 
 static bool br_supported(const pnb_params& p) {
@@ -545,11 +575,11 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
   if (rc) return rc;
   switch (K->p.pbs_level) {
     case 1: break;
-    case 2: return launch_ml<2>(K, tv, small, out, count, tb, st);
-    case 3: return launch_ml<3>(K, tv, small, out, count, tb, st);
-    case 4: return launch_ml<4>(K, tv, small, out, count, tb, st);
-    case 5: return launch_ml<5>(K, tv, small, out, count, tb, st);
-    case 6: return launch_ml<6>(K, tv, small, out, count, tb, st);
+    case 2: return launch_ml_any<2, 15>(K, tv, small, out, count, tb, st);
+    case 3: return launch_ml_any<3, 11>(K, tv, small, out, count, tb, st);
+    case 4: return launch_ml_any<4, 10>(K, tv, small, out, count, tb, st);
+    case 5: return launch_ml_any<5, 8>(K, tv, small, out, count, tb, st);
+    case 6: return launch_ml_any<6, 7>(K, tv, small, out, count, tb, st);
     default:
       set_error("blind rotation: pbs_level %d not compiled", K->p.pbs_level);
       return PNB_ERR_UNSUPPORTED;

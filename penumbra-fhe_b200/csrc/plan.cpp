@@ -201,7 +201,10 @@ struct Builder {
     P.code.push_back(std::move(I));
     P.pbs_per_sample += count;
     P.cost_per_sample += (double)count * o.levels[level].cost;
+    if ((int)per_level.size() < (int)o.levels.size()) per_level.assign(o.levels.size(), 0);
+    per_level[level] += count;
   }
+  std::vector<int64_t> per_level;
 
   // Remove the low `k` bits of the running value in buffer R (count elements, LSB scale E,
   // variance V) LSB-first, then leave it ready for a final read of cell 2^(64-bf) at scale
@@ -648,7 +651,12 @@ struct Builder {
     }
     P.output_elems = out_off;
     rep << "bootstraps per sample: " << P.pbs_per_sample << " (cost " << P.cost_per_sample
-        << " single-level equivalents)\n";
+        << " single-level equivalents)";
+    for (size_t l = 0; l < per_level.size(); ++l)
+      if (per_level[l])
+        rep << (l ? ", " : "; ") << "(2^" << o.levels[l].base_log << "," << o.levels[l].level
+            << "): " << per_level[l];
+    rep << "\n";
     P.report = rep.str();
   }
 
