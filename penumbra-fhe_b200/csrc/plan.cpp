@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstdio>
+#include <functional>
 #include <map>
 #include <numeric>
 #include <sstream>
@@ -78,8 +79,8 @@ std::vector<KeyLevel> default_levels(int n, int N, int k, double glwe_std) {
   };
   // noise measured on a B200 over 4096 bootstraps; cost = measured time per bootstrap
   // relative to the single-level kernel
-  static const Row rows[] = {{23, 1, 49.1, 1.0}, {15, 2, 41.9, 5.6}, {11, 3, 38.7, 10.2},
-                             {10, 4, 36.6, 12.8}, {7, 6, 33.9, 30.8}};
+  static const Row rows[] = {{23, 1, 49.1, 1.0}, {15, 2, 41.9, 6.3}, {11, 3, 38.7, 10.4},
+                             {10, 4, 36.6, 14.4}, {7, 6, 33.9, 20.9}};
   const bool is_default = (n == 834 && N == 2048 && k == 1 &&
                            std::fabs(glwe_std - 2.845267479601915e-15) < 1e-20);
   std::vector<KeyLevel> out;
@@ -122,6 +123,7 @@ struct Builder {
   std::vector<int> scale;
   std::vector<double> vmax, var;
   std::vector<int> buf;
+  std::vector<std::vector<int64_t>> k0s;  // per threshold node (see thresholds())
 
   Builder(const ir::Graph& gr, const Options& op) : g(gr), o(op) {}
 
@@ -206,27 +208,20 @@ struct Builder {
   }
   std::vector<int64_t> per_level;
 
-  // Remove the low `k` bits of the running value in buffer R (count elements, LSB scale E,
-  // variance V) LSB-first, then leave it ready for a final read of cell 2^(64-bf) at scale
-  // E+k.  Returns false when the noise budget cannot be met.
+  // A digit chain: the running value in buffer R (count elements per sample) at LSB scale
+  // 2^E with noise variance V; X is the bootstrap output scratch (same element count).
   struct Chain {
-    int R;  // running value
-    int X;  // bootstrap output scratch (same element count)
+    int R;
+    int X;
     int64_t count;
     int E;
     double V;
   };
-  std::vector<int> split(int k) {
-    std::vector<int> w;
-    while (k > 0) {
-      w.push_back(std::min(k, 5));
-      k -= w.back();
-    }
-    return w;
-  }
-  bool plan_windows(Chain c, int k, int final_cell, std::vector<int>* lv, double* Vend,
-                    double* cost) {
-    std::vector<int> ws = split(k);
+
+  // Key sets for a given window sequence (LSB first): each bootstrap takes the cheapest key
+  // whose output keeps the next read within its budget.  False when some read is over budget.
+  bool eval_windows(const Chain& c, const std::vector<int>& ws, int final_cell,
+                    std::vector<int>* lv, double* Vend, double* cost) const {
     // read sequence: (cell, E) per read; pbs i adds noise before read i+1
     std::vector<std::pair<int, int>> reads;
     int E = c.E;
@@ -254,8 +249,45 @@ struct Builder {
     *Vend = V;
     return true;
   }
-  void emit_windows(Chain& c, int k, const std::vector<int>& lv, const std::string& what) {
-    std::vector<int> ws = split(k);
+
+  // Remove the low k bits: the cheapest split into windows of 1..5 bits (every split for
+  // k <= 17; for wider chains the first 12 bits are searched and the rest taken in fives).
+  bool plan_windows(Chain c, int k, int final_cell, std::vector<int>* lv, double* Vend,
+                    double* cost, std::vector<int>* ws_out = nullptr) {
+    const int head = k <= 17 ? k : 12;
+    std::vector<int> tail;
+    for (int r = k - head; r > 0; r -= std::min(r, 5)) tail.push_back(std::min(r, 5));
+    std::vector<int> cur, best_ws, best_lv, tmp_lv;
+    double best = 1e300, best_V = 0;
+    std::function<void(int)> rec = [&](int left) {
+      if (left == 0) {
+        std::vector<int> ws = cur;
+        ws.insert(ws.end(), tail.begin(), tail.end());
+        double V, cst;
+        if (eval_windows(c, ws, final_cell, &tmp_lv, &V, &cst) && cst < best - 1e-9) {
+          best = cst;
+          best_ws = ws;
+          best_lv = tmp_lv;
+          best_V = V;
+        }
+        return;
+      }
+      for (int w = std::min(5, left); w >= 1; --w) {
+        cur.push_back(w);
+        rec(left - w);
+        cur.pop_back();
+      }
+    };
+    rec(head);
+    if (best >= 1e300) return false;
+    *lv = best_lv;
+    *Vend = best_V;
+    *cost = best;
+    if (ws_out) *ws_out = best_ws;
+    return true;
+  }
+  void emit_windows(Chain& c, const std::vector<int>& ws, const std::vector<int>& lv,
+                    const std::string& what) {
     const int X = c.X;
     size_t li = 0;
     for (int w : ws) {
@@ -399,10 +431,13 @@ struct Builder {
   }
 
   // thresholds of a Requant / Argmax node, per element
+  // k0[e]: the clamp index every y of element e reaches (c0 plus the thresholds decided as
+  // crossed); the output is clamp_lut[k0 + number of undecided thresholds crossed].
   void thresholds(const ir::Node& nd, const std::vector<Range>& y, std::vector<Pair>* pairs,
-                  std::vector<int64_t>* base) {
+                  std::vector<int64_t>* base, std::vector<int64_t>* k0 = nullptr) {
     const auto& op = nd.op;
     base->assign(y.size(), 0);
+    if (k0) k0->assign(y.size(), 0);
     pairs->clear();
     for (size_t e = 0; e < y.size(); ++e) {
       if (op.type == OpType::Argmax) {
@@ -421,6 +456,7 @@ struct Builder {
       const int64_t M = (1 << op.out_bits) - 1;
       const int64_t c0 = s >= 64 ? 0 : (int64_t)std::min<uint64_t>(rb >> s, (uint64_t)M);
       int64_t b = (int64_t)op.clamp_lut[c0];
+      int64_t kk = c0;
       for (int64_t j = c0 + 1; j <= M; ++j) {
         const int64_t delta = (int64_t)op.clamp_lut[j] - (int64_t)op.clamp_lut[j - 1];
         // y >= T  <=>  mult*y + rb >= j*2^s  (for y >= 0; j*2^s > rb so T > 0)
@@ -428,11 +464,13 @@ struct Builder {
         const i128 T = ceil_div(num, (i128)mult);
         if (T <= y[e].lo) {
           b += delta;
+          ++kk;
         } else if (T <= y[e].hi && delta != 0) {
           pairs->push_back({(int)e, (int)j, (int64_t)T, delta});
         }
       }
       (*base)[e] = b;
+      if (k0) (*k0)[e] = kk;
     }
   }
 
@@ -501,10 +539,11 @@ struct Builder {
     // per threshold node: pairs and base
     std::vector<std::vector<Pair>> pairs(g.nodes.size());
     std::vector<std::vector<int64_t>> bases(g.nodes.size());
+    k0s.assign(g.nodes.size(), {});
     for (size_t ni = 0; ni < g.nodes.size(); ++ni) {
       const auto& nd = g.nodes[ni];
       if (nd.op.type == OpType::Requant || nd.op.type == OpType::Argmax)
-        thresholds(nd, range[tensor(nd.inputs[0])], &pairs[ni], &bases[ni]);
+        thresholds(nd, range[tensor(nd.inputs[0])], &pairs[ni], &bases[ni], &k0s[ni]);
     }
 
     // scale of each class: the widest signed range any member (or chain on it) must hold
@@ -836,7 +875,9 @@ struct Builder {
     chain_bits(vr, &ky, &bfy);
     std::vector<int> lvy;
     double Vy_end = 0, costy = 0;
-    const bool y_ok = plan_windows(Chain{-1, -1, 0, ey, var[in]}, ky, 64 - bfy, &lvy, &Vy_end, &costy);
+    std::vector<int> wsy, wsA, wsB;
+    const bool y_ok =
+        plan_windows(Chain{-1, -1, 0, ey, var[in]}, ky, 64 - bfy, &lvy, &Vy_end, &costy, &wsy);
     const int fl = out_level(out, per_elem, nd.name);
     costy = (costy + o.levels[fl].cost) * pairs.size();
 
@@ -898,14 +939,16 @@ struct Builder {
         }
         const int cellA = z_lut ? lut_cell : (kB > 0 ? 64 - std::min(kB, 5) : 64 - bfB);
         double costA = 0;
-        if (plan_windows(Chain{-1, -1, 0, ey, m2 * var[in]}, s, cellA, &lvA, &VA_end, &costA)) {
+        if (plan_windows(Chain{-1, -1, 0, ey, m2 * var[in]}, s, cellA, &lvA, &VA_end, &costA,
+                         &wsA)) {
           if (z_lut) {
             const int lz = out_level(out, 1, nd.name);
             costz = (costA + o.levels[lz].cost) * zel.size();
             z_ok = true;
           } else {
             double VB_end = 0, costB = 0;
-            if (plan_windows(Chain{-1, -1, 0, ey + s, VA_end}, kB, 64 - bfB, &lvB, &VB_end, &costB)) {
+            if (plan_windows(Chain{-1, -1, 0, ey + s, VA_end}, kB, 64 - bfB, &lvB, &VB_end,
+                             &costB, &wsB)) {
               costz = costA * zel.size() + (costB + o.levels[fl].cost) * pairs.size();
               z_ok = true;
             }
@@ -941,7 +984,7 @@ struct Builder {
       }
       lin(RA, {Term{buf[in], coef, map}}, c, nd.name + ": z = mult*y + rb");
       Chain ch{RA, XA, nz, ey, m2 * var[in]};
-      emit_windows(ch, s, lvA, nd.name + " (z)");
+      emit_windows(ch, wsA, lvA, nd.name + " (z)");
       if (z_lut) {
         // q = z >> shift sits at scale 2^(ey+s): one lookup gives the whole output
         int lb = 0;
@@ -997,13 +1040,13 @@ struct Builder {
       }
       lin(RB, {Term{RA, {1}, pm}}, pc, nd.name + ": per threshold");
       Chain cb{RB, XB, np, ey + s, ch.V};
-      emit_windows(cb, kB, lvB, nd.name + " (q)");
-      finish_pairs(cb, bfB, pairs, out, cst, fl, nd.name);
+      emit_windows(cb, wsB, lvB, nd.name + " (q)");
+      const std::string fin = finish_pairs(cb, bfB, pairs, out, cst, fl, nd.name, ni);
       snprintf(line, sizeof line,
                "%-20s Requant    z-space: %zu elems remove %d bits, %zu pairs remove %d more "
-               "(%zu+%zu bootstraps, final key (%d,%d))\n",
+               "(%zu+%zu bootstraps), %s\n",
                nd.name.c_str(), zel.size(), s, pairs.size(), kB, lvA.size(), lvB.size() + 1,
-               o.levels[fl].base_log, o.levels[fl].level);
+               fin.c_str());
       rep << line;
       return;
     }
@@ -1018,35 +1061,31 @@ struct Builder {
     }
     lin(R, {Term{buf[in], {1}, pm}}, pc, nd.name + ": v = y - T");
     Chain c{R, Xv, np, ey, var[in]};
-    emit_windows(c, ky, lvy, nd.name);
-    finish_pairs(c, bfy, pairs, out, cst, fl, nd.name);
+    emit_windows(c, wsy, lvy, nd.name);
+    const std::string fin = finish_pairs(c, bfy, pairs, out, cst, fl, nd.name, ni);
     std::string levels;
-    for (int l : lvy)
-      levels += "(" + std::to_string(o.levels[l].base_log) + "," + std::to_string(o.levels[l].level) + ")";
-    snprintf(line, sizeof line,
-             "%-20s %-10s y-space: %zu pairs remove %d bits [%s] + final sign key (%d,%d)\n",
-             nd.name.c_str(), op.name(), pairs.size(), ky, levels.c_str(), o.levels[fl].base_log,
-             o.levels[fl].level);
+    for (int l : lvy) levels += key_name(l);
+    snprintf(line, sizeof line, "%-20s %-10s y-space: %zu pairs remove %d bits [%s], %s\n",
+             nd.name.c_str(), op.name(), pairs.size(), ky, levels.c_str(), fin.c_str());
     rep << line;
   }
 
-  // final sign read of every pair and the telescoped sum into the output tensor
-  void finish_pairs(const Chain& c, int bf, const std::vector<Pair>& pairs, int out,
-                    std::vector<uint64_t>& cst, int fl, const std::string& name) {
+  // Final sign read of every pair, then either
+  //  (direct)   out = base + sum_j delta_j [v_j >= 0], each sign bootstrap emitting its term at
+  //             the output scale with the key the output's consumers need, or
+  //  (combined) each sign bootstrap emits a bit at 2^61 with the cheapest key, the bits of an
+  //             element are summed into k (the undecided thresholds crossed), and one lookup
+  //             bootstrap with the consumers' key emits clamp_lut[k0 + k] -- one precise
+  //             bootstrap per element instead of one per threshold.
+  std::string key_name(int l) const {
+    return "(" + std::to_string(o.levels[l].base_log) + "," + std::to_string(o.levels[l].level) +
+           ")";
+  }
+  // returns a description of the final stage for the plan report
+  std::string finish_pairs(const Chain& c, int bf, const std::vector<Pair>& pairs, int out,
+                           std::vector<uint64_t>& cst, int fl, const std::string& name, int ni) {
     const int64_t np = (int64_t)pairs.size();
     const int ex = scale[out];
-    std::vector<int32_t> tvi(np);
-    std::map<int64_t, int> tv_of_delta;
-    for (int64_t p = 0; p < np; ++p) {
-      const int64_t d = pairs[p].delta;
-      auto it = tv_of_delta.find(d);
-      if (it == tv_of_delta.end())
-        it = tv_of_delta.emplace(d, tv(const_tv((uint64_t)d << (ex - 1)))).first;
-      tvi[p] = it->second;
-      cst[pairs[p].e] += (uint64_t)d << (ex - 1);
-    }
-    const int X = c.X;
-    pbs(X, c.R, 64 - bf - c.E, pow2(63 - bf), fl, tvi, np, name + ": final sign");
     const int64_t E = (int64_t)cst.size();
     std::vector<std::vector<int32_t>> maps;
     std::vector<int> cnt(E, 0);
@@ -1056,10 +1095,86 @@ struct Builder {
       if ((int)maps.size() <= t) maps.emplace_back(E, -1);
       maps[t][e] = (int32_t)p;
     }
+    const int J = (int)maps.size();
+    const auto& op = g.nodes[ni].op;
+    // combined form: bits read back at cells of 2^61 (k <= 3 fits four cells)
+    int lb = -1, ll = -1;
+    int64_t ne = 0;
+    for (int64_t e = 0; e < E; ++e) ne += cnt[e] > 0;
+    if (op.type == OpType::Requant && J >= 2) {
+      lb = pick(0, allowed(61, 61) / J);
+      for (int l : lvl_order)
+        if (lvar(l) <= vmax[out]) {
+          ll = l;
+          break;
+        }
+    }
+    const double cost_direct = (double)np * o.levels[fl].cost;
+    const double cost_comb = (lb < 0 || ll < 0) ? 1e300
+                                                : (double)np * o.levels[lb].cost +
+                                                      (double)ne * o.levels[ll].cost;
+    const int X = c.X;
+    if (cost_comb >= cost_direct) {
+      std::vector<int32_t> tvi(np);
+      std::map<int64_t, int> tv_of_delta;
+      for (int64_t p = 0; p < np; ++p) {
+        const int64_t d = pairs[p].delta;
+        auto it = tv_of_delta.find(d);
+        if (it == tv_of_delta.end())
+          it = tv_of_delta.emplace(d, tv(const_tv((uint64_t)d << (ex - 1)))).first;
+        tvi[p] = it->second;
+        cst[pairs[p].e] += (uint64_t)d << (ex - 1);
+      }
+      pbs(X, c.R, 64 - bf - c.E, pow2(63 - bf), fl, tvi, np, name + ": final sign");
+      std::vector<Term> terms;
+      for (auto& m : maps) terms.push_back(Term{X, {1}, m});
+      lin(buf[out], terms, cst, name + ": sum of thresholds");
+      var[out] = (double)J * lvar(fl);
+      return "final signs " + key_name(fl);
+    }
+    pbs(X, c.R, 64 - bf - c.E, pow2(63 - bf), lb, {tv(const_tv(pow2(60)))}, np,
+        name + ": final sign (bit)");
+    // S[i] = k_i * 2^61 over the elements with undecided thresholds
+    std::vector<int32_t> elem_of(ne), idx_of(E, -1);
+    {
+      int64_t i = 0;
+      for (int64_t e = 0; e < E; ++e)
+        if (cnt[e] > 0) {
+          idx_of[e] = (int32_t)i;
+          elem_of[i++] = (int32_t)e;
+        }
+    }
+    const int S = new_buf(ne, name + ".count");
+    const int Y = new_buf(ne, name + ".lookup");
     std::vector<Term> terms;
-    for (auto& m : maps) terms.push_back(Term{X, {1}, m});
-    lin(buf[out], terms, cst, name + ": sum of thresholds");
-    var[out] = (double)maps.size() * lvar(fl);
+    for (auto& m : maps) {
+      std::vector<int32_t> mi(ne);
+      for (int64_t i = 0; i < ne; ++i) mi[i] = m[elem_of[i]];
+      terms.push_back(Term{X, {1}, mi});
+    }
+    std::vector<uint64_t> sc(ne);
+    for (int64_t i = 0; i < ne; ++i) sc[i] = (uint64_t)cnt[elem_of[i]] << 60;
+    lin(S, terms, sc, name + ": count of thresholds crossed");
+    const int64_t M = (1 << op.out_bits) - 1;
+    std::map<int64_t, int> tv_of_k0;
+    std::vector<int32_t> tvi(ne);
+    for (int64_t i = 0; i < ne; ++i) {
+      const int64_t k0 = k0s[ni][elem_of[i]];
+      auto it = tv_of_k0.find(k0);
+      if (it == tv_of_k0.end()) {
+        TvSpec sp;
+        sp.lut_len = 4;
+        for (int k = 0; k < 4; ++k) sp.val.push_back(op.clamp_lut[std::min<int64_t>(k0 + k, M)] << ex);
+        it = tv_of_k0.emplace(k0, tv(sp)).first;
+      }
+      tvi[i] = it->second;
+    }
+    pbs(Y, S, 0, 0, ll, tvi, ne, name + ": clamp lookup of the count");
+    std::vector<uint64_t> oc(E);
+    for (int64_t e = 0; e < E; ++e) oc[e] = idx_of[e] >= 0 ? 0 : cst[e];
+    lin(buf[out], {Term{Y, {1}, idx_of}}, oc, name + ": assemble");
+    var[out] = lvar(ll);
+    return "final sign bits " + key_name(lb) + " + one lookup " + key_name(ll);
   }
 };
 
