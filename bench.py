@@ -266,6 +266,45 @@ def noise_leg(pnb, keys, dev, total=100352):
             "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2))}
 
 
+def mlp_cpu_baseline(plan, graph, per_level: int = 32):
+    """CPU restatement of the same encrypted MLP program, timed on a bounded sample.
+
+    Every key set the program uses gets `per_level` oracle f64-FFT bootstraps (keyswitch +
+    blind rotation + extraction, all host threads); the first layer's contraction is timed on
+    one sample.  Samples/s = 1 / (sum over key sets of count x seconds per bootstrap +
+    contraction seconds)."""
+    import numpy as np
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    threads = os.cpu_count() or 1
+    rng = np.random.default_rng(SEED + 11)
+    sec = 0.0
+    timed = []
+    for base_log, level, count in plan.key_sets():
+        p = O.default_params()
+        p.pbs_base_log, p.pbs_level = base_log, level
+        keys = O.OracleKeys(p, SEED)
+        _ = keys.fbsk
+        ct = keys.encrypt_big(rng.integers(0, 16, per_level), seed=SEED + 12)
+        tv = keys.test_vector(rng.integers(0, 16, 16))
+        keys.pbs_fft(ct[:2], tv, threads=threads)
+        t0 = time.perf_counter()
+        keys.pbs_fft(ct, tv, threads=threads)
+        t = (time.perf_counter() - t0) / per_level
+        sec += count * t
+        timed.append(f"({base_log},{level}): {count} x {1e3 * t:.2f} ms")
+    W = np.array(graph["nodes"][0]["op"]["weights"], dtype=np.int64)
+    X = rng.integers(0, 1 << 63, (1, W.shape[1], 2049), dtype=np.uint64)
+    t0 = time.perf_counter()
+    O.contract(W, None, 0, X, threads=threads)
+    tc = time.perf_counter() - t0
+    sec += tc
+    return {"value": 1.0 / sec, "unit": "samples/s", "cores": threads, "kind": "port",
+            "sample": f"{per_level} oracle bootstraps per key set, extrapolated by the "
+                      f"program's counts [{'; '.join(timed)}] + the 784->128 contraction of one "
+                      f"sample ({1e3 * tc:.1f} ms)"}
+
+
 def mlp_leg(args, pnb, world, rank, local, dist, dev):
     """Encrypted MLP inference over a sample shard per rank; returns the "mlp" object."""
     import numpy as np
@@ -332,6 +371,10 @@ def mlp_leg(args, pnb, world, rank, local, dist, dev):
                    "parallelism": f"samples sharded over {world} GPU(s), outputs all-gathered "
                                   "over NCCL"},
         "bootstraps_per_sample": plan.pbs_per_sample,
+        "bootstraps_by_key_set": [{"base_log": b, "levels": l, "per_sample": c}
+                                  for b, l, c in plan.key_sets()],
+        "cpu_baseline": (mlp_cpu_baseline(plan, graph)
+                         if rank == 0 and world == 1 and not args.no_cpu_baseline else None),
         "allgather_ms": t_gather,
         "e2e": {"value": world * B / (t_e2e * 1e-3), "unit": "samples/s",
                 "h2d_bytes_per_step": int(h_in.numel() * 8),

@@ -209,6 +209,9 @@ int pnb_plan_info(const pnb_plan* plan, pnb_plan_summary* info);
  * tensor idx.  Encrypt inputs at 2^scale_log2; decode outputs by signed rounding at 2^scale_log2. */
 int pnb_plan_tensor(const pnb_plan* plan, int is_output, int idx, int64_t* elems,
                     int* scale_log2, int64_t* lo, int64_t* hi);
+/* Key sets (gadget base_log, levels) the program bootstraps with and the bootstraps per sample
+ * of each; fills up to `cap` entries and returns the number of key sets (-1 on a bad argument). */
+int pnb_plan_key_sets(const pnb_plan* plan, int cap, int* base_log, int* level, int64_t* count);
 /* Human-readable program summary (bytes needed including the terminator). */
 size_t pnb_plan_report(const pnb_plan* plan, char* buf, size_t cap);
 /* Noise-free host execution of the program on cleartext integers: inputs [batch][input_elems],

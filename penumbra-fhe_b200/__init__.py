@@ -101,6 +101,8 @@ _SIGS = {
                                   C.POINTER(C.c_int), C.POINTER(C.c_int64),
                                   C.POINTER(C.c_int64)]),
     "pnb_plan_report": (C.c_size_t, [C.c_void_p, C.c_char_p, C.c_size_t]),
+    "pnb_plan_key_sets": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                    C.POINTER(C.c_int64)]),
     "pnb_plan_simulate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
                                     C.POINTER(C.c_double)]),
     "pnb_evaluator_create": (C.c_int, [C.c_void_p, C.c_int, C.c_uint64, C.c_size_t,
@@ -503,6 +505,13 @@ class Plan:
         _check("pnb_plan_tensor", lib().pnb_plan_tensor(self._h, is_out, i, C.byref(e),
                                                         C.byref(sc), C.byref(lo), C.byref(hi)))
         return {"elems": e.value, "scale": sc.value, "lo": lo.value, "hi": hi.value}
+
+    def key_sets(self) -> list[tuple[int, int, int]]:
+        """(base_log, levels, bootstraps per sample) of every key set the program uses."""
+        n = lib().pnb_plan_key_sets(self._h, 0, None, None, None)
+        b, l, c = (C.c_int * n)(), (C.c_int * n)(), (C.c_int64 * n)()
+        lib().pnb_plan_key_sets(self._h, n, b, l, c)
+        return [(b[i], l[i], c[i]) for i in range(n)]
 
     def report(self) -> str:
         n = lib().pnb_plan_report(self._h, None, 0)

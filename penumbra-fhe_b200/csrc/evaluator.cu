@@ -408,6 +408,25 @@ int pnb_plan_tensor(const pnb_plan* p, int is_output, int idx, int64_t* elems, i
   return PNB_OK;
 }
 
+int pnb_plan_key_sets(const pnb_plan* p, int cap, int* base_log, int* level, int64_t* count) {
+  if (!p || cap < 0) {
+    set_error("pnb_plan_key_sets: bad argument");
+    return -1;
+  }
+  const auto& P = p->prog;
+  int n = 0;
+  for (size_t l = 0; l < P.pbs_per_level.size(); ++l) {
+    if (!P.pbs_per_level[l]) continue;
+    if (n < cap) {
+      if (base_log) base_log[n] = P.levels[l].base_log;
+      if (level) level[n] = P.levels[l].level;
+      if (count) count[n] = P.pbs_per_level[l];
+    }
+    ++n;
+  }
+  return n;
+}
+
 size_t pnb_plan_report(const pnb_plan* p, char* buf, size_t cap) {
   if (!p) return 0;
   const std::string& r = p->prog.report;

@@ -205,6 +205,7 @@ struct Builder {
     P.cost_per_sample += (double)count * o.levels[level].cost;
     if ((int)per_level.size() < (int)o.levels.size()) per_level.assign(o.levels.size(), 0);
     per_level[level] += count;
+    P.pbs_per_level = per_level;
   }
   std::vector<int64_t> per_level;
 

@@ -109,6 +109,7 @@ struct Program {
   int64_t input_elems = 0, output_elems = 0;  // per sample, all tensors concatenated
   int64_t pbs_per_sample = 0;
   double cost_per_sample = 0;
+  std::vector<int64_t> pbs_per_level;  // bootstraps per sample by key set (indexes levels)
   std::string report;
   Options opt;
 };
