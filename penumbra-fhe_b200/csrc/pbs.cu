@@ -381,16 +381,17 @@ constexpr int BR_CPB = 4;
 // 64-thread block, warp p owning accumulator polynomial p (u64 words: the gadget digits need
 // base_log * level > 32 bits of it).  Per CMux and level the warp forms its digit polynomial,
 // transforms it, exchanges the spectrum with the other warp in two 8 KB halves and accumulates
-// D_own * F[own row][p] + D_other * F[other row][p]; levels 0..L-2 accumulate in shared memory,
-// the last in registers, which then go through the inverse transform.  About 99 KB of shared
-// memory per block: two blocks (four warps) per SM.
+// D_own * F[own row][p] + D_other * F[other row][p].  The sums of levels 0..L-2 live in tensor
+// memory (128 columns per block: warp p uses lanes 32p..32p+31, four columns per spectrum row),
+// the last level's in registers, which then go through the inverse transform.  Shared memory
+// holds only the accumulator, the scratch halves and the ciphertext's rotation amounts (about
+// 51 KB), so four blocks (eight warps) run per SM; the forward twiddles come through L1.
 struct BrMlSmem {
   uint64_t acc[2][FFT_N];    // 32 KB accumulator (mask, body)
-  double2 facc[2][FFT_M];    // 32 KB spectrum partial sums over the first L-1 levels
   double scratch[2][FFT_M];  // 16 KB transpose / exchange halves, one per warp
-  double2 wf[FFT_M];         // 16 KB forward twiddles
   double2 twf[32], twi[32];
   uint16_t abar[BR_MAXN];
+  uint32_t tmem_holder;
 };
 
 // Balanced base-2^beta digit `lev` (0 = most significant) of the top beta*L bits of v, rounded:
@@ -419,7 +420,7 @@ __device__ __forceinline__ double2 ld_key_stream(const double2* p) {
 }
 
 template <int L, int BETA>
-__global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
+__global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel,
     const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
     int base_log, FftTables tb) {
@@ -432,7 +433,7 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
   const uint64_t* tv = tv_of(sel, ct);
   constexpr int LG = 12;
   for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
-  for (int e = threadIdx.x; e < FFT_M; e += 64) S.wf[e] = tb.wf[e];
+  if (warp == 0) tc::tmem_alloc(tc::smem_u32(&S.tmem_holder), 128);
   if (threadIdx.x < 32) {
     S.twf[threadIdx.x] = tb.twf[threadIdx.x];
     S.twi[threadIdx.x] = tb.twi[threadIdx.x];
@@ -443,12 +444,16 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     S.acc[0][t] = 0;
     S.acc[1][t] = rot_coef(tv, t, r0);
   }
+  tc::tc_fence_before();
   __syncthreads();
+  tc::tc_fence_after();
+  // this warp's lane quarter; column 4r + {0..3} holds the double2 of spectrum row r
+  const uint32_t tfacc = *reinterpret_cast<volatile uint32_t*>(&S.tmem_holder) +
+                         ((uint32_t)(32 * p) << 16);
   uint64_t* my0 = S.acc[p];
   double* buf0 = S.scratch[p];
   double2* xch0 = reinterpret_cast<double2*>(S.scratch[p]);
   const double2* och0 = reinterpret_cast<const double2*>(S.scratch[p ^ 1]);
-  double2* facc0 = S.facc[p];
   const double2* wi_g = tb.wi;
 
   for (int i = 0; i < n; ++i) {
@@ -466,8 +471,7 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
       double* buf = buf0;
       double2* xch = xch0;
       const double2* och = och0;
-      double2* facc = facc0;
-      if (L > 2) asm volatile("" : "+l"(my), "+l"(buf), "+l"(xch), "+l"(och), "+l"(facc));
+      if (L > 2) asm volatile("" : "+l"(my), "+l"(buf), "+l"(xch), "+l"(och));
 #pragma unroll
       for (int m = 0; m < 32; ++m) {
         if ((m & 7) == 0) asm volatile("" ::: "memory");
@@ -477,7 +481,7 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
         x[m] = make_double2((double)ml_digit<L, BETA>(v0, base_log, lev),
                             (double)ml_digit<L, BETA>(v1, base_log, lev));
       }
-      fft_forward_h(x, buf, lane, S.wf, S.twf);
+      fft_forward_h(x, buf, lane, tb.wf, S.twf);
       const double2* f_own = ggsw + ((size_t)(p * L + lev) * 2 + p) * FFT_M;
       const double2* f_oth = ggsw + ((size_t)((p ^ 1) * L + lev) * 2 + p) * FFT_M;
       const bool last = lev == L - 1;
@@ -487,23 +491,40 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
         for (int rr = 0; rr < 16; ++rr) xch[rr * 32 + lane] = x[16 * h + rr];
         pair_sync(0);
 #pragma unroll
-        for (int rr = 0; rr < 16; ++rr) {
-          const int r = 16 * h + rr;
-          const int e = r * 32 + lane;
-          const double2 fo = ld_key_stream(&f_own[e]), ft = ld_key_stream(&f_oth[e]);
-          const double2 dt = och[rr * 32 + lane];
-          const double2 p0 = cmul(x[r], fo);
-          double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
-                                   p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+        for (int g4 = 0; g4 < 4; ++g4) {
+          const int rb = 16 * h + 4 * g4;  // four spectrum rows = 16 TMEM columns
+          uint32_t t[16];
           if (lev > 0) {
-            const double2 o = facc[e];
-            v = make_double2(v.x + o.x, v.y + o.y);
+            tc::tmem_ld_32x32_x16(tfacc + (uint32_t)(4 * rb), t);
+            tc::tmem_ld_wait();
           }
-          if (last) x[r] = v;
-          else facc[e] = v;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int r = rb + q;
+            const int e = r * 32 + lane;
+            const double2 fo = ld_key_stream(&f_own[e]), ft = ld_key_stream(&f_oth[e]);
+            const double2 dt = och[(r - 16 * h) * 32 + lane];
+            const double2 p0 = cmul(x[r], fo);
+            double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
+                                     p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+            if (lev > 0) {
+              v.x += __hiloint2double((int)t[4 * q + 1], (int)t[4 * q + 0]);
+              v.y += __hiloint2double((int)t[4 * q + 3], (int)t[4 * q + 2]);
+            }
+            if (last) {
+              x[r] = v;
+            } else {
+              t[4 * q + 0] = (uint32_t)__double2loint(v.x);
+              t[4 * q + 1] = (uint32_t)__double2hiint(v.x);
+              t[4 * q + 2] = (uint32_t)__double2loint(v.y);
+              t[4 * q + 3] = (uint32_t)__double2hiint(v.y);
+            }
+          }
+          if (!last) tc::tmem_st_32x32_x16(tfacc + (uint32_t)(4 * rb), t);
         }
         pair_sync(0);
       }
+      if (!last) tc::tmem_st_wait();
     }
     fft_inverse_h(x, buf0, lane, wi_g, S.twi);
 #pragma unroll
@@ -515,7 +536,12 @@ __global__ void __launch_bounds__(64, 2) blind_rotate_ml_kernel(
     }
     __syncwarp();
   }
+  tc::tc_fence_before();
   __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(&S.tmem_holder), 128);
+  }
   uint64_t* o = out + (size_t)ct * (FFT_N + 1);
   for (int t = threadIdx.x; t < FFT_N; t += 64)
     o[t] = (t == 0) ? S.acc[0][0] : (uint64_t)0 - S.acc[0][FFT_N - t];
