@@ -16,7 +16,7 @@ quantized by the reference quantizer, tests/golden/cfg4_mlp.json) evaluated end 
 encryption -- the whole graph, every Linear on the tensor cores and every Requant as an exact
 bootstrap program -- on `--mlp-batch` synthetic samples per GPU (seeded uniform 6-bit inputs).
 
-Also in the line: "contraction" -- the encrypted Linear 784->128 (int4 weights, 256 samples of
+Also in the line: "pbs_batch_sweep" -- PBS/s at batch sizes 1 to 65536; "contraction" -- the encrypted Linear 784->128 (int4 weights, 256 samples of
 784 ciphertexts) on the tensor cores against the HBM roofline; "noise" -- the single-level
 bootstrap's output noise over ~1e5 bootstraps beside its analytic value.
 
@@ -231,6 +231,38 @@ def _measured_hbm():
     except Exception:
         pass
     return {"value": 6650.0, "source": "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"}
+
+
+def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 65536)):
+    """PBS/s (keyswitch + blind rotation, device-timed, inputs resident) across batch sizes."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(SEED + 21)
+    tv = pnb.test_vector(keys, rng.integers(0, 16, 16))
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for B in batches:
+        ct = pnb.encrypt(keys, torch.tensor(rng.integers(0, 16, B)), seed=SEED + 22)
+        small = torch.empty((B, keys.params.n + 1), dtype=torch.int64, device=dev)
+        ks_ws = torch.empty(pnb.keyswitch_workspace_bytes(keys, B), dtype=torch.uint8, device=dev)
+        o = torch.empty_like(ct)
+        reps = 3 if B >= 4096 else 5
+        pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+        pnb.blind_rotate(keys, tv, small, out=o)
+        ms = 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+            pnb.blind_rotate(keys, tv, small, out=o)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms += a.elapsed_time(b)
+        ms /= reps
+        out.append({"batch": B, "pbs_per_second": B / (ms * 1e-3), "ms": ms})
+        del ct, small, ks_ws, o
+    return out
 
 
 def noise_leg(pnb, keys, dev, total=100352):
@@ -484,6 +516,7 @@ def run_gpu(args):
     contraction = None if args.contract_batch <= 0 else contraction_leg(args, pnb, local, dev,
                                                                            flush)
     noise = noise_leg(pnb, keys, dev) if (rank == 0 and args.noise) else None
+    sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -514,6 +547,7 @@ def run_gpu(args):
             "mlp": mlp,
             "contraction": contraction,
             "noise": noise,
+            "pbs_batch_sweep": sweep,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -533,6 +567,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--contract-batch", type=int, default=256,
                     help="samples of the Linear 784->128 contraction leg (0 skips it)")
+    ap.add_argument("--sweep", type=int, default=1,
+                    help="PBS/s across batch sizes 1..65536 (rank 0)")
     ap.add_argument("--noise", type=int, default=1,
                     help="measure the bootstrap output noise over ~1e5 bootstraps (rank 0)")
     ap.add_argument("--mlp-batch", type=int, default=32,

@@ -124,6 +124,9 @@ struct Builder {
   std::vector<double> vmax, var;
   std::vector<int> buf;
   std::vector<std::vector<int64_t>> k0s;  // per threshold node (see thresholds())
+  // Share of a bootstrap read's noise budget granted to the value it reads (the rest is left to
+  // the bootstrap outputs the chain adds before its next read).
+  double vfrac = 0.5;
 
   Builder(const ir::Graph& gr, const Options& op) : g(gr), o(op) {}
 
@@ -632,11 +635,11 @@ struct Builder {
           int k, bf;
           chain_bits(v, &k, &bf);
           const int cell = k > 0 ? 64 - std::min(k, 5) : 64 - bf;
-          vmax[in] = std::min(vmax[in], 0.5 * allowed(cell, scale[in]));
+          vmax[in] = std::min(vmax[in], vfrac * allowed(cell, scale[in]));
           break;
         }
         case OpType::Activation: {
-          vmax[in] = std::min(vmax[in], 0.5 * allowed(act_cell(range[in]), scale[in]));
+          vmax[in] = std::min(vmax[in], vfrac * allowed(act_cell(range[in]), scale[in]));
           break;
         }
       }
@@ -1182,9 +1185,27 @@ struct Builder {
 }  // namespace
 
 Program build(const ir::Graph& g, const Options& o) {
-  Builder b(g, o);
-  b.run();
-  return std::move(b.P);
+  // How much of a chain's first read budget goes to its input (and so how precise the key sets
+  // producing that input must be) trades cost between layers: try a few splits, keep the
+  // cheapest program.
+  Program best;
+  bool have = false;
+  std::string first_error;
+  for (double f : {0.5, 0.6, 0.7, 0.8}) {
+    try {
+      Builder b(g, o);
+      b.vfrac = f;
+      b.run();
+      if (!have || b.P.cost_per_sample < best.cost_per_sample) {
+        best = std::move(b.P);
+        have = true;
+      }
+    } catch (const Error& e) {
+      if (first_error.empty()) first_error = e.what();
+    }
+  }
+  if (!have) throw Error(first_error);
+  return best;
 }
 
 // ---- noise-free execution ------------------------------------------------------------

@@ -133,3 +133,37 @@ def test_max_pool_is_reported_unsupported(pnb):
                     "pool_h": 2, "pool_w": 2, "stride": 2}}], ["x"], ["y"], 6, 5)
     with pytest.raises(pnb.LibraryError, match="max"):
         pnb.Plan(pnb.Graph(g), input_range=(-31, 31))
+
+
+def _linear_requant_graph():
+    # Encrypted Linear 784 -> 128 with int4 weights U[-8, 7] and 6-bit inputs, followed by a
+    # ReLU-fused requantization to 2 bits (the synthetic Linear + Requant configuration)
+    rng = np.random.default_rng(3)
+    W = rng.integers(-8, 8, (128, 784)).tolist()
+    nodes = [{"name": "fc", "inputs": ["x"], "outputs": ["acc"],
+              "op": {"op_type": "Linear", "weights": W, "bias": [0] * 128, "weight_bits": 4}},
+             {"name": "rq", "inputs": ["acc"], "outputs": ["y"],
+              "op": _requant(11, mult=1, rb=1024)}]
+    return _g(nodes, ["x"], ["y"], 12, 6)
+
+
+def test_linear_requant_program(pnb):
+    g = _linear_requant_graph()
+    plan = pnb.Plan(pnb.Graph(g))
+    xs = np.random.default_rng(4).integers(0, 64, (6, 784))
+    y, margin = plan.simulate(xs)
+    for x, got in zip(xs, y):
+        assert got.tolist() == ir_eval.evaluate(g, {"x": x.tolist()})["y"]
+    assert margin >= 63.5
+
+
+@pytest.mark.gpu
+def test_linear_requant_encrypted(pnb):
+    g = _linear_requant_graph()
+    plan = pnb.Plan(pnb.Graph(g))
+    ev = pnb.Evaluator(plan, device=0, seed=17)
+    xs = np.random.default_rng(5).integers(0, 64, (4, 784))
+    got = ev.decrypt(ev.evaluate(ev.encrypt(xs, seed=6))).cpu().numpy()
+    for x, row in zip(xs, got):
+        assert row.tolist() == ir_eval.evaluate(g, {"x": x.tolist()})["y"]
+    assert pnb.device_status(0) == 0
