@@ -1,5 +1,5 @@
-// lwe.cu -- LWE phase (client decrypt), the ciphertext x cleartext-weight contraction, and the
-// FP64 throughput probe used as the blind rotation's roofline denominator.
+// lwe.cu -- LWE phase (client decrypt) and the FP64 throughput probe used as the blind
+// rotation's roofline denominator.  (The contraction is in contract_tc.cu.)
 #include <cstdio>
 
 #include "pnb_internal.cuh"
@@ -27,72 +27,6 @@ int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count,
   const uint64_t* key = small ? K->lwe_sk : K->glwe_sk;
   phase_kernel<<<(count + 7) / 8, 256, 0, st>>>(ct, key, dim, phase, count);
   PNB_CHECK_LAUNCH("phase_kernel");
-  return PNB_OK;
-}
-
-// ------------------------------------------------------------------------------------------
-// Contraction Y[b][j][c] = sum_i W[j][i] X[b][i][c] (+ bias[j]*delta on the body column).
-// CUDA-core version: a block owns (sample b, 32 output rows, 256 columns); each thread owns
-// one column and 32 row accumulators; W rows of the tile are staged in shared memory.
-// ------------------------------------------------------------------------------------------
-constexpr int CT_ROWS = 32;
-constexpr int CT_COLS = 256;
-constexpr int CT_KCH = 64;
-
-__global__ void __launch_bounds__(CT_COLS) contract_kernel(
-    const int8_t* __restrict__ W, const int64_t* __restrict__ bias, uint64_t delta, int M, int K,
-    const uint64_t* __restrict__ X, uint64_t* __restrict__ Y, int lwe_len) {
-  __shared__ int32_t ws[CT_ROWS][CT_KCH];
-  const int b = blockIdx.z;
-  const int j0 = blockIdx.y * CT_ROWS;
-  const int c = blockIdx.x * CT_COLS + threadIdx.x;
-  const int rows = min(CT_ROWS, M - j0);
-  uint64_t acc[CT_ROWS];
-#pragma unroll
-  for (int r = 0; r < CT_ROWS; ++r) acc[r] = 0;
-  const uint64_t* xb = X + (size_t)b * K * lwe_len;
-  for (int k0 = 0; k0 < K; k0 += CT_KCH) {
-    __syncthreads();
-    for (int e = threadIdx.x; e < CT_ROWS * CT_KCH; e += CT_COLS) {
-      const int r = e / CT_KCH, kk = e % CT_KCH;
-      ws[r][kk] = (r < rows && k0 + kk < K) ? (int32_t)W[(size_t)(j0 + r) * K + k0 + kk] : 0;
-    }
-    __syncthreads();
-    if (c < lwe_len) {
-      const int kmax = min(CT_KCH, K - k0);
-      for (int kk = 0; kk < kmax; ++kk) {
-        const uint64_t x = __ldg(xb + (size_t)(k0 + kk) * lwe_len + c);
-#pragma unroll
-        for (int r = 0; r < CT_ROWS; ++r) acc[r] += (uint64_t)(int64_t)ws[r][kk] * x;
-      }
-    }
-  }
-  if (c < lwe_len) {
-#pragma unroll
-    for (int r = 0; r < CT_ROWS; ++r) {
-      if (r < rows) {
-        uint64_t v = acc[r];
-        if (bias && c == lwe_len - 1) v += (uint64_t)bias[j0 + r] * delta;
-        Y[((size_t)b * M + j0 + r) * lwe_len + c] = v;
-      }
-    }
-  }
-}
-
-int lwe_contract(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
-                 const uint64_t* X, uint64_t* Y, int batch, int lwe_len, cudaStream_t st) {
-  if (M <= 0 || K <= 0 || batch < 0 || lwe_len <= 0) {
-    set_error("lwe_contract: bad shape M=%d K=%d batch=%d lwe_len=%d", M, K, batch, lwe_len);
-    return PNB_ERR_INVALID;
-  }
-  if (batch == 0) return PNB_OK;
-  if (batch > 65535) {
-    set_error("lwe_contract: batch %d exceeds the grid limit of 65535 per call", batch);
-    return PNB_ERR_INVALID;
-  }
-  dim3 grid((lwe_len + CT_COLS - 1) / CT_COLS, (M + CT_ROWS - 1) / CT_ROWS, batch);
-  contract_kernel<<<grid, CT_COLS, 0, st>>>(W, bias, delta, M, K, X, Y, lwe_len);
-  PNB_CHECK_LAUNCH("contract_kernel");
   return PNB_OK;
 }
 

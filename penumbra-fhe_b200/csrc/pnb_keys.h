@@ -42,8 +42,6 @@ int encrypt_lwe(const pnb_keys* K, const int64_t* msg, uint64_t delta, uint64_t 
                 uint64_t first, uint64_t* ct, int count, cudaStream_t st);
 int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count, int small,
               cudaStream_t st);
-int lwe_contract(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
-                 const uint64_t* X, uint64_t* Y, int batch, int lwe_len, cudaStream_t st);
 int measure_fp64_peak(double* tflops);
 int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                     const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st);
