@@ -373,18 +373,33 @@ struct Builder {
             for (int oy = 0; oy < oh; ++oy)
               for (int ox = 0; ox < ow; ++ox) {
                 i128 lo = 0, hi = 0;
+                bool first = true;
                 for (int ky = 0; ky < op.pool_h; ++ky)
                   for (int kx = 0; kx < op.pool_w; ++kx) {
                     const Range& r = X[(size_t)c * op.in_h * op.in_w +
                                        (oy * op.stride + ky) * op.in_w + ox * op.stride + kx];
-                    lo += r.lo;
-                    hi += r.hi;
+                    if (op.pool_avg) {
+                      lo += r.lo;
+                      hi += r.hi;
+                    } else {
+                      lo = first ? r.lo : std::max<i128>(lo, r.lo);
+                      hi = first ? r.hi : std::max<i128>(hi, r.hi);
+                    }
+                    first = false;
                   }
                 R[(c * oh + oy) * ow + ox] = {to_i64(lo, where), to_i64(hi, where)};
               }
-          if (!op.pool_avg)
-            fail("Pool mode \"max\" is not implemented on this path (node '" + nd.name +
-                 "'); use \"avg\"");
+          if (!op.pool_avg) {
+            int64_t lo = INT64_MAX, hi = INT64_MIN;
+            for (const auto& r : X) {
+              lo = std::min(lo, r.lo);
+              hi = std::max(hi, r.hi);
+            }
+            if (hi - lo > 3)
+              fail("node '" + nd.name + "': max pooling is implemented for inputs that take at "
+                   "most four values (a 2-bit activation); this input spans [" +
+                   std::to_string(lo) + ", " + std::to_string(hi) + "]");
+          }
           break;
         }
         case OpType::Requant: {
@@ -420,8 +435,8 @@ struct Builder {
           break;
         }
       }
-      if (op.type == OpType::Linear || op.type == OpType::Conv2d || op.type == OpType::Pool ||
-          op.type == OpType::Add)
+      if (op.type == OpType::Linear || op.type == OpType::Conv2d ||
+          (op.type == OpType::Pool && op.pool_avg) || op.type == OpType::Add)
         unite(t, tensor(nd.inputs[0]));
       range[t] = std::move(R);
       if (op.type == OpType::Linear || op.type == OpType::Conv2d) {
@@ -563,7 +578,8 @@ struct Builder {
       const int yt = tensor(nd.inputs[0]);
       for (const Pair& p : pairs[ni])
         tighten(yt, range[yt][p.e].lo - p.T, range[yt][p.e].hi - p.T);
-      if (nd.op.type == OpType::Activation) cap[find(yt)] = std::min(cap[find(yt)], 59);
+      if (nd.op.type == OpType::Activation || (nd.op.type == OpType::Pool && !nd.op.pool_avg))
+        cap[find(yt)] = std::min(cap[find(yt)], 59);
     }
     // A Requant reading a class rooted at a graph input sees fresh (tiny) noise, so the single
     // z = mult*y + rb chain is affordable there: leave room for z's wider range.
@@ -620,7 +636,10 @@ struct Builder {
           break;
         }
         case OpType::Pool:
-          vmax[in] = std::min(vmax[in], vmax[out] / (op.pool_h * op.pool_w));
+          if (op.pool_avg)
+            vmax[in] = std::min(vmax[in], vmax[out] / (op.pool_h * op.pool_w));
+          else  // read as 4a + b at cells of 2^59 (see emit_maxpool)
+            vmax[in] = std::min(vmax[in], 0.9 * allowed(59, scale[in]) / 17.0);
           break;
         case OpType::Add:
           vmax[in] = std::min(vmax[in], vmax[out] / 2);
@@ -737,6 +756,10 @@ struct Builder {
       case OpType::Linear:
       case OpType::Conv2d:
       case OpType::Pool: {
+        if (op.type == OpType::Pool && !op.pool_avg) {
+          emit_maxpool(ni, rep);
+          return;
+        }
         Instr I;
         I.kind = Kind::Contract;
         I.dst = buf[out];
@@ -844,6 +867,101 @@ struct Builder {
         emit_threshold(ni, pairs, base, rep);
         return;
     }
+  }
+
+  // Max pooling of a tensor whose values span at most four integers [lo, lo+3] (a 2-bit
+  // activation): a pairwise tree, max(a, b) = one 16-entry lookup bootstrap on
+  // 4(a - lo) + (b - lo) read at cells of 2^59; inner results carry max - lo at scale 2^57.
+  void emit_maxpool(int ni, std::ostringstream& rep) {
+    const auto& nd = g.nodes[ni];
+    const auto& op = nd.op;
+    const int out = tensor(nd.outputs[0]);
+    const int in = tensor(nd.inputs[0]);
+    const int64_t E = (int64_t)range[out].size();
+    const int ex = scale[in], eo = scale[out];
+    int64_t lo = INT64_MAX;
+    for (const auto& r : range[in]) lo = std::min(lo, r.lo);
+    const int oh = (op.in_h - op.pool_h) / op.stride + 1;
+    const int ow = (op.in_w - op.pool_w) / op.stride + 1;
+    // operand t of output o: (buffer, element map, scale, offset removed?)
+    struct Opd {
+      int buf;
+      std::vector<int32_t> map;  // per output element
+      int scale;
+      bool leaf;
+    };
+    std::vector<Opd> ops;
+    for (int ky = 0; ky < op.pool_h; ++ky)
+      for (int kx = 0; kx < op.pool_w; ++kx) {
+        Opd d{buf[in], std::vector<int32_t>(E), ex, true};
+        for (int c = 0; c < op.channels; ++c)
+          for (int oy = 0; oy < oh; ++oy)
+            for (int ox = 0; ox < ow; ++ox)
+              d.map[(c * oh + oy) * ow + ox] = c * op.in_h * op.in_w +
+                                               (oy * op.stride + ky) * op.in_w + ox * op.stride +
+                                               kx;
+        ops.push_back(std::move(d));
+      }
+    const double tmp_lim = 0.9 * allowed(59, 59) / 272.0;  // inner results read with 16 and 4
+    int inner = -1;
+    for (int l : lvl_order)
+      if (lvar(l) <= tmp_lim) {
+        inner = l;
+        break;
+      }
+    if (inner < 0) fail("node '" + nd.name + "': no key set is precise enough for max pooling");
+    const int fl = out_level(out, 1, nd.name);
+    int level_no = 0;
+    int64_t pbs_count = 0;
+    if (ops.size() == 1) {
+      // a 1x1 window: rescale through an identity lookup
+      TvSpec sp;
+      sp.lut_len = 4;
+      for (int v = 0; v < 4; ++v) sp.val.push_back((uint64_t)(v + lo) << eo);
+      const int X = new_buf(E, nd.name + ".in");
+      lin(X, {Term{ops[0].buf, {(int64_t)pow2(61 - ex)}, ops[0].map}},
+          {(uint64_t)0 - ((uint64_t)lo << 61)}, nd.name + ": stage");
+      pbs(buf[out], X, 0, 0, fl, {tv(sp)}, E, nd.name + ": identity lookup");
+      var[out] = lvar(fl);
+      return;
+    }
+    while (ops.size() > 1) {
+      const size_t np = ops.size() / 2;
+      const bool last = ops.size() == 2;
+      std::vector<Opd> next;
+      for (size_t j = 0; j < np; ++j) {
+        const Opd& a = ops[2 * j];
+        const Opd& b = ops[2 * j + 1];
+        const int D = new_buf(E, nd.name + ".pair");
+        uint64_t c = 0;
+        if (a.leaf) c -= (uint64_t)lo << 61;
+        if (b.leaf) c -= (uint64_t)lo << 59;
+        lin(D, {Term{a.buf, {(int64_t)pow2(61 - a.scale)}, a.map},
+                Term{b.buf, {(int64_t)pow2(59 - b.scale)}, b.map}},
+            {c}, nd.name + ": 4a + b");
+        TvSpec sp;
+        sp.lut_len = 16;
+        for (int v = 0; v < 16; ++v) {
+          const int m = std::max(v >> 2, v & 3);
+          sp.val.push_back(last ? (uint64_t)(m + lo) << eo : (uint64_t)m << 57);
+        }
+        const int Y = last ? buf[out] : new_buf(E, nd.name + ".max");
+        pbs(Y, D, 0, 0, last ? fl : inner, {tv(sp)}, E, nd.name + ": pairwise max");
+        pbs_count += E;
+        std::vector<int32_t> id(E);
+        for (int64_t e = 0; e < E; ++e) id[e] = (int32_t)e;
+        next.push_back(Opd{Y, id, 57, false});
+      }
+      if (ops.size() % 2) next.push_back(ops.back());
+      ops = std::move(next);
+      ++level_no;
+    }
+    var[out] = lvar(fl);
+    char line[256];
+    snprintf(line, sizeof line, "%-20s Pool(max)  %lld bootstraps/elem over %d tree levels, key %s\n",
+             nd.name.c_str(), (long long)(pbs_count / std::max<int64_t>(E, 1)), level_no,
+             key_name(fl).c_str());
+    rep << line;
   }
 
   void emit_threshold(int ni, const std::vector<Pair>& pairs, const std::vector<int64_t>& base,

@@ -167,3 +167,42 @@ def test_linear_requant_encrypted(pnb):
     for x, row in zip(xs, got):
         assert row.tolist() == ir_eval.evaluate(g, {"x": x.tolist()})["y"]
     assert pnb.device_status(0) == 0
+
+
+def _maxpool_graph():
+    # Conv2d -> ReLU-Requant -> 2x2 max pool (stride 2) -> Linear head
+    rng = np.random.default_rng(8)
+    conv = _conv(rng.integers(-7, 8, (3, 9)).tolist(), [4, -6, 0], 6, 6, 1, 3, 1, 1)
+    nodes = [{"name": "conv", "inputs": ["x"], "outputs": ["c"], "op": conv},
+             {"name": "rq", "inputs": ["c"], "outputs": ["r"], "op": _requant(6, mult=3, rb=32)},
+             {"name": "mp", "inputs": ["r"], "outputs": ["m"],
+              "op": {"op_type": "Pool", "mode": "max", "in_h": 6, "in_w": 6, "channels": 3,
+                     "pool_h": 2, "pool_w": 2, "stride": 2}},
+             {"name": "fc", "inputs": ["m"], "outputs": ["y"],
+              "op": {"op_type": "Linear", "weights": rng.integers(-7, 8, (4, 27)).tolist(),
+                     "bias": [1, 2, 3, 4], "weight_bits": 4}}]
+    return _g(nodes, ["x"], ["m", "y"], 10, 4)
+
+
+def test_max_pool_program(pnb):
+    g = _maxpool_graph()
+    plan = pnb.Plan(pnb.Graph(g))
+    xs = np.random.default_rng(9).integers(0, 16, (8, 36))
+    y, margin = plan.simulate(xs)
+    for x, got in zip(xs, y):
+        r = ir_eval.evaluate(g, {"x": x.tolist()})
+        assert got.tolist() == r["m"] + r["y"]
+    assert margin >= 63.5
+
+
+@pytest.mark.gpu
+def test_max_pool_encrypted(pnb):
+    g = _maxpool_graph()
+    plan = pnb.Plan(pnb.Graph(g))
+    ev = pnb.Evaluator(plan, device=0, seed=23)
+    xs = np.random.default_rng(10).integers(0, 16, (5, 36))
+    got = ev.decrypt(ev.evaluate(ev.encrypt(xs, seed=2))).cpu().numpy()
+    for x, row in zip(xs, got):
+        r = ir_eval.evaluate(g, {"x": x.tolist()})
+        assert row.tolist() == r["m"] + r["y"]
+    assert pnb.device_status(0) == 0
