@@ -14,11 +14,11 @@ re-evaluates the reference's committed fixtures (``examples/mnist/phase2_fixture
 
 Only this script reads the reference; tests and the GPU box read the JSON it writes.
 
-Config 4 and 5 need the quantizer workaround recorded in the survey: the reference's
-``insert_requants`` sizes requantized accumulators from the un-requantized graph and rejects
-them at the final radix; requants are inserted at the 64-block probe width and the graph is then
-given the minimal width computed on the requantized graph (the reference's own
-``Model._minimal_num_blocks``).
+The MLP and CNN graphs need a quantizer workaround: the reference's ``insert_requants``
+(``python/penumbra/compile.py:184``) sizes requantized accumulators from the un-requantized
+graph and rejects them at the final radix; requants are inserted at the 64-block probe width
+and the graph is then given the minimal width computed on the requantized graph (the
+reference's own ``Model._minimal_num_blocks``, ``python/penumbra/model.py:354-369``).
 """
 from __future__ import annotations
 
