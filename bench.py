@@ -274,6 +274,7 @@ def noise_leg(pnb, keys, dev, total=100352):
     lut = rng.integers(0, 16, 16)
     tv = pnb.test_vector(keys, lut)
     errs = []
+    first = None
     n = 0
     while n < total:
         msgs = rng.integers(0, 16, B)
@@ -282,8 +283,19 @@ def noise_leg(pnb, keys, dev, total=100352):
         ph = pnb.phase(keys, out).cpu().numpy()
         want = (lut[msgs].astype(np.uint64) * np.uint64(keys.params.delta()))
         errs.append((ph.view(np.uint64) - want).view(np.int64).astype(np.float64))
+        if first is None:
+            first = (ct[:1024].cpu().numpy().view(np.uint64), lut, msgs[:1024])
         n += B
     e = np.concatenate(errs)
+    # the CPU restatement's bootstrap on the first 1024 inputs, same keys (same seed)
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    ok = O.OracleKeys(O.default_params(), SEED)
+    cts, lut0, m0 = first
+    ref = ok.pbs_fft(cts, ok.test_vector(lut0), threads=os.cpu_count() or 1)
+    e_ref = (ok.phase_big(ref) - lut0[m0].astype(np.uint64) * np.uint64(keys.params.delta()))
+    e_ref = e_ref.view(np.int64).astype(np.float64)
+    e_gpu = e[:1024]
     # analytic variance of the same blind rotation (key noise through the digits + gadget
     # rounding), for comparison
     p = keys.params
@@ -294,6 +306,9 @@ def noise_leg(pnb, keys, dev, total=100352):
     v2 = (p.n / 2) * (1 + p.k * p.N / 2) * eps * eps / 12
     return {"bootstraps": int(e.size), "log2_std": float(np.log2(e.std())),
             "mean_over_std": float(e.mean() / e.std()),
+            "variance_ratio_vs_cpu_restatement": float(e_gpu.var() / e_ref.var()),
+            "cpu_restatement_log2_std": float(np.log2(e_ref.std())),
+            "ratio_sample": "first 1024 bootstraps, identical keys and ciphertexts",
             "analytic_log2_std": float(0.5 * np.log2(v1 + v2)),
             "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2))}
 
