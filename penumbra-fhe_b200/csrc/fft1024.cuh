@@ -1,22 +1,27 @@
 // fft1024.cuh -- warp-level negacyclic FFT for polynomials of size N = 2048.
 //
-// A real polynomial a(X) mod X^N + 1 is folded into M = N/2 complex points
-//   y_j = a_j + i a_{j+M},   z_j = y_j * zeta^j,   zeta = exp(i pi / N),
-// whose M-point DFT evaluates a(X) at the M roots zeta^(1-4t) of X^N + 1 (those with
-// X^(N/2) = i); the conjugate roots follow from a being real.  Products of such transforms are
-// negacyclic products.  This is the same "folding" evaluation tfhe-rs performs with its f64
-// FFT (tfhe-fft 0.10.1), restated for one warp:
+// A real polynomial a(X) mod X^N + 1 is folded into M = N/2 complex coefficients
+//   y_j = a_j + i a_{j+M},
+// and the transform evaluates y at the M roots rho of X^M = i (a(rho) = y(rho) there; the other
+// half of the roots of X^N + 1 are their conjugates, redundant for a real a).  Products of such
+// evaluations are negacyclic products.  This is the "folding" evaluation tfhe-rs performs with
+// its f64 FFT (tfhe-fft 0.10.1), restated for one warp:
 //
-//   M = 1024 = 32 x 32 (four-step).  Lane l holds y_{l + 32 m} in register m.
-//   forward : twist by zeta^{32 m} (per register) -> in-register DFT32 over m (DIF, output
-//             bit-reversed) -> twiddle zeta^l W^{l k2} -> shared-memory transpose ->
-//             in-register DFT32 (DIF).  Result: lane l, register r holds
-//             Z[32 bitrev(r) + bitrev(l)]  (the "permuted spectrum" order).
-//   inverse : exactly the mirror (DIT stages with conjugate twiddles), taking the permuted
-//             spectrum back to y'_{l + 32 n} in lane l, register n, scaled by 1/M.
+//   M = 1024 = 32 x 32.  Lane l holds y_{l + 32 m} in register m.
+//   forward : per lane, the 32-point evaluation of sum_m y_{l+32m} X^m at the 32 roots sigma_r of
+//             X^32 = i, by the Cooley-Tukey reduction tree X^32 - i -> (X^16 - s)(X^16 + s) ...
+//             (natural input, roots in bit-reversed order; the twist by the 1024th root is part
+//             of the tree's twiddles) -> twiddle rho_r^l, rho_r = exp(i pi (1 + 4 br(r)) / 2048)
+//             -> shared-memory transpose -> the same tree for X^32 - 1.  Result: lane r,
+//             register s holds y(rho_r w^br(s)), w = exp(2 pi i / 32), br = 5-bit reversal.
+//   inverse : per lane, a decimation-in-time DFT32 (bit-reversed input, natural output) ->
+//             conjugate twiddle -> transpose -> DFT32 -> untwist exp(-i pi m / 64) / 1024.
 //
-// No bit reversal is ever materialised: pointwise products happen in the permuted order, and
-// the Fourier bootstrapping key is produced by the same forward routine.
+// Every butterfly has the form (u + w v, u - w v) with the twiddle w ahead of the sum, so each
+// one with a non-trivial w is six FMAs (Linzer-Feig: w v = A v (1 + iB) or A v (B + i)); a
+// butterfly with w in {1, i, -1, -i} is four adds.  No bit reversal is materialised: pointwise
+// products happen in the spectrum order above, and the Fourier bootstrapping key is produced by
+// the same forward routine.
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -29,101 +34,129 @@ constexpr int FFT_R = 32;       // registers (complex) per lane
 constexpr int FFT_M = 1024;     // complex points per polynomial
 constexpr int FFT_N = 2048;     // polynomial size
 
-// Twiddle tables for one device (all in device global memory).
+// Twiddle tables between the two 32-point passes (device global memory, one set per device).
 struct FftTables {
-  double2* wf;   // [r*32 + l] = zeta^l * W^{l * bitrev(r)}         (forward, between steps)
-  double2* wi;   // [n*32 + l] = zeta^{-n} * W^{-n * bitrev(l)}       (inverse, between steps)
-  double2* twf;  // [m] = zeta^{32 m}                                 (forward pre-twist)
-  double2* twi;  // [n] = zeta^{-32 n} / M                            (inverse post-twist)
+  double2* wf;  // [r*32 + l] = T(r, l) = rho_r^l                 (forward: lane l, register r)
+  double2* wi;  // [n*32 + l] = conj(T(l, n))                      (inverse: lane l, register n)
 };
 
-// Read-only load the compiler may not hoist out of the blind-rotation loop: the twiddles are
-// loop-invariant, and keeping all of them in registers across iterations would spill.
-__device__ __forceinline__ double2 ld_tw(const double2* p) {
-  double2 v;
-  asm volatile("ld.global.nc.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
-  return v;
+__host__ __device__ constexpr int bitrev_bits(int v, int bits) {
+  int r = 0;
+  for (int b = 0; b < bits; ++b)
+    if (v & (1 << b)) r |= 1 << (bits - 1 - b);
+  return r;
 }
 
 __device__ __forceinline__ double2 cmul(double2 a, double2 b) {
   return make_double2(fma(a.x, b.x, -a.y * b.y), fma(a.x, b.y, a.y * b.x));
 }
-__device__ __forceinline__ double2 cmul_conj(double2 a, double c, double s) {
-  // a * (c - i s)
-  return make_double2(fma(a.x, c, a.y * s), fma(a.y, c, -a.x * s));
-}
-__device__ __forceinline__ double2 cmul_cs(double2 a, double c, double s) {
-  // a * (c + i s)
-  return make_double2(fma(a.x, c, -a.y * s), fma(a.x, s, a.y * c));
+// a * conj(b)
+__device__ __forceinline__ double2 cmul_conj(double2 a, double2 b) {
+  return make_double2(fma(a.x, b.x, a.y * b.y), fma(a.y, b.x, -a.x * b.y));
 }
 
-// One radix-2 stage of span LEN over the 32 registers.  Templated so that every register
-// index is a compile-time constant (a runtime stage length would demote x[] to local memory).
-template <int LEN>
-__device__ __forceinline__ void dif_stage(double2 (&x)[FFT_R]) {
-  constexpr int HALF = LEN / 2;
+// (u, v) <- (u + w v, u - w v), w = exp(2 pi i e / 128).  `e` is a compile-time constant after
+// unrolling, so every branch below folds away.  CB selects where the factors come from: the
+// constant bank (operands of the FMAs themselves) or literals (materialised in uniform
+// registers); which one leaves fewer general registers live depends on the kernel around it.
+template <bool CB>
+__device__ __forceinline__ void ct_bfly(int e, double2& u, double2& v) {
+  e &= 127;
+  double px, py;  // w v, or w v / A in the fused forms
+  if (e % 32 == 0) {
+    if (e == 0) { px = v.x; py = v.y; }
+    else if (e == 32) { px = -v.y; py = v.x; }
+    else if (e == 64) { px = -v.x; py = -v.y; }
+    else { px = v.y; py = -v.x; }
+    const double2 a = u;
+    u = make_double2(a.x + px, a.y + py);
+    v = make_double2(a.x - px, a.y - py);
+    return;
+  }
+  double A, B;
+  if (CB) {
+    A = kLF128[e].x;
+    B = kLF128[e].y;
+  } else {
+    lf128_lit(e, A, B);
+  }
+  if (lf_tan_form(e)) {  // w v = A (v.x - B v.y, v.y + B v.x)
+    px = fma(-B, v.y, v.x);
+    py = fma(B, v.x, v.y);
+  } else {               // w v = A (B v.x - v.y, B v.y + v.x)
+    px = fma(B, v.x, -v.y);
+    py = fma(B, v.y, v.x);
+  }
+  const double2 a = u;
+  u = make_double2(fma(A, px, a.x), fma(A, py, a.y));
+  v = make_double2(fma(-A, px, a.x), fma(-A, py, a.y));
+}
+
+// Stage K (1..5) of the reduction tree of X^32 - exp(2 pi i TH0 / 128): node g splits
+// X^(2h) - c into X^h - s and X^h + s, s = sqrt(c) = exp(2 pi i (TH0 + 128 br(g)) / 2^K / 128).
+template <int K, int TH0, bool CB>
+__device__ __forceinline__ void crt_stage(double2 (&x)[FFT_R]) {
+  constexpr int H = 32 >> K;
 #pragma unroll
-  for (int s = 0; s < 32; s += LEN) {
+  for (int g = 0; g < (1 << (K - 1)); ++g) {
+    const int e = (TH0 + 128 * bitrev_bits(g, K - 1)) >> K;
 #pragma unroll
-    for (int j = 0; j < HALF; ++j) {
-      const double2 u = x[s + j], v = x[s + j + HALF];
-      x[s + j] = make_double2(u.x + v.x, u.y + v.y);
-      const double2 d = make_double2(u.x - v.x, u.y - v.y);
-      const int k = j * (32 / LEN);  // W_LEN^j = W32^k
-      if (k == 0) {
-        x[s + j + HALF] = d;
-      } else if (k == 8) {  // -i
-        x[s + j + HALF] = make_double2(d.y, -d.x);
-      } else {
-        double c, sn;
-        w32(k, c, sn);
-        x[s + j + HALF] = cmul_cs(d, c, sn);
-      }
-    }
+    for (int j = 0; j < H; ++j) ct_bfly<CB>(e, x[2 * H * g + j], x[2 * H * g + j + H]);
   }
 }
 
-template <int LEN>
-__device__ __forceinline__ void dit_stage_inv(double2 (&x)[FFT_R]) {
-  constexpr int HALF = LEN / 2;
+// Evaluation of sum_m x_m X^m at the roots of X^32 = exp(2 pi i TH0 / 128): register r ends up
+// holding the value at exp(2 pi i (TH0 / 32 + 4 br(r)) / 128).
+template <int TH0, bool CB>
+__device__ __forceinline__ void crt_dft32(double2 (&x)[FFT_R]) {
+  crt_stage<1, TH0, CB>(x);
+  crt_stage<2, TH0, CB>(x);
+  crt_stage<3, TH0, CB>(x);
+  crt_stage<4, TH0, CB>(x);
+  crt_stage<5, TH0, CB>(x);
+}
+
+// Decimation-in-time stage of span 2^K: twiddle exp(-2 pi i j / 2^K) on the upper element.
+template <int K, bool CB>
+__device__ __forceinline__ void dit_stage(double2 (&x)[FFT_R]) {
+  constexpr int LEN = 1 << K, HALF = LEN / 2;
 #pragma unroll
   for (int s = 0; s < 32; s += LEN) {
 #pragma unroll
-    for (int j = 0; j < HALF; ++j) {
-      const int k = j * (32 / LEN);
-      const double2 u = x[s + j], v = x[s + j + HALF];
-      double2 t;
-      if (k == 0) {
-        t = v;
-      } else if (k == 8) {  // conj(-i) = +i
-        t = make_double2(-v.y, v.x);
-      } else {
-        double c, sn;
-        w32(k, c, sn);
-        t = cmul_conj(v, c, sn);
-      }
-      x[s + j] = make_double2(u.x + t.x, u.y + t.y);
-      x[s + j + HALF] = make_double2(u.x - t.x, u.y - t.y);
-    }
+    for (int j = 0; j < HALF; ++j) ct_bfly<CB>(128 - j * (128 >> K), x[s + j], x[s + j + HALF]);
   }
 }
 
-// Forward DFT32, decimation in frequency: natural input, bit-reversed output.
-__device__ __forceinline__ void dft32_dif(double2 (&x)[FFT_R]) {
-  dif_stage<32>(x);
-  dif_stage<16>(x);
-  dif_stage<8>(x);
-  dif_stage<4>(x);
-  dif_stage<2>(x);
+// out_k = sum_n in_n exp(-2 pi i n k / 32) with in_n in register br(n), out_k in register k.
+template <bool CB>
+__device__ __forceinline__ void dit_dft32(double2 (&x)[FFT_R]) {
+  dit_stage<1, CB>(x);
+  dit_stage<2, CB>(x);
+  dit_stage<3, CB>(x);
+  dit_stage<4, CB>(x);
+  dit_stage<5, CB>(x);
 }
 
-// Inverse DFT32 (exponent +), decimation in time: bit-reversed input, natural output. Unscaled.
-__device__ __forceinline__ void idft32_dit(double2 (&x)[FFT_R]) {
-  dit_stage_inv<2>(x);
-  dit_stage_inv<4>(x);
-  dit_stage_inv<8>(x);
-  dit_stage_inv<16>(x);
-  dit_stage_inv<32>(x);
+// x_m *= exp(-2 pi i m / 128) * 2^-SHIFT, SHIFT = 10 (the 1/M) or 42 (also the 2^-32 the blind
+// rotation's rounding expects); the constants come pre-scaled.
+template <int SHIFT, bool CB>
+__device__ __forceinline__ void untwist(double2 (&x)[FFT_R]) {
+  static_assert(SHIFT == 10 || SHIFT == 42, "untwist tables exist for 2^-10 and 2^-42");
+  const double2* k = SHIFT == 10 ? kUntwist10 : kUntwist42;
+  constexpr double sc = 1.0 / (double)(1ull << SHIFT);
+#pragma unroll
+  for (int m = 0; m < 32; ++m) {
+    double c, sn;
+    if (CB) {
+      c = k[m].x;
+      sn = k[m].y;
+    } else {
+      cs128_lit((128 - m) & 127, c, sn);
+      c *= sc;  // literals: folded at compile time
+      sn *= sc;
+    }
+    x[m] = m == 0 ? make_double2(x[m].x * c, x[m].y * c) : cmul(x[m], make_double2(c, sn));
+  }
 }
 
 // Swizzled 32x32 transpose through a per-warp shared buffer of 1024 double2.
@@ -153,83 +186,85 @@ __device__ __forceinline__ void warp_transpose_half(double2 (&x)[FFT_R], double*
   __syncwarp();
 }
 
-// Forward / inverse FFT through the 8 KB half buffer.  The forward twiddles come from shared
-// memory (`wf_s`, `twf_s`); the inverse ones from the cached global table and `twi_s`.
-__device__ __forceinline__ void fft_forward_h(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const double2* wf_s, const double2* twf_s) {
-#pragma unroll
-  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], twf_s[m]);
-  dft32_dif(x);
-#pragma unroll
-  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], wf_s[r * 32 + lane]);
-  warp_transpose_half(x, buf, lane);
-  dft32_dif(x);
+// Read-only load the compiler may not hoist out of the blind-rotation loop: the twiddles are
+// loop-invariant, and keeping all of them in registers across iterations would spill.
+__device__ __forceinline__ double2 ld_tw(const double2* p) {
+  double2 v;
+  asm volatile("ld.global.nc.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
+  return v;
 }
 
-__device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const double2* wi_g, const double2* twi_s) {
-  idft32_dit(x);
-#pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&wi_g[n * 32 + lane]));
-  warp_transpose_half(x, buf, lane);
-  idft32_dit(x);
-#pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], twi_s[n]);
-}
-
-// Forward twiddle table held once in shared memory for both directions.  Element (a, b) of the
-// 32x32 table lives at a*32 + ((a+b) & 31): the forward FFT reads row r across the lanes and the
-// inverse reads the transpose (its twiddle (n, lane) is the conjugate of forward element
-// (lane, n)); with this swizzle both patterns are bank-conflict free.
-__device__ __forceinline__ int tw_swz(int a, int b) { return a * 32 + ((a + b) & 31); }
-
-__device__ __forceinline__ void fft_forward_s(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const double2* wf_sw, const double2* twf_s) {
-#pragma unroll
-  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], twf_s[m]);
-  dft32_dif(x);
-#pragma unroll
-  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], wf_sw[tw_swz(r, lane)]);
-  warp_transpose_half(x, buf, lane);
-  dft32_dif(x);
-}
-
-__device__ __forceinline__ void fft_inverse_s(double2 (&x)[FFT_R], double* buf, int lane,
-                                              const double2* wf_sw, const double2* twi_s) {
-  idft32_dit(x);
-#pragma unroll
-  for (int n = 0; n < 32; ++n) {
-    const double2 w = wf_sw[tw_swz(lane, n)];  // inverse twiddle = conj(w)
-    x[n] = make_double2(fma(x[n].x, w.x, x[n].y * w.y), fma(x[n].x, -w.y, x[n].y * w.x));
-  }
-  warp_transpose_half(x, buf, lane);
-  idft32_dit(x);
-#pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], twi_s[n]);
-}
-
-// Forward negacyclic FFT of one folded polynomial (see header comment).
+// Forward transform with the twiddles T from global memory (through L1) and a 16 KB buffer.
+template <bool CB = true>
 __device__ __forceinline__ void fft_forward(double2 (&x)[FFT_R], double2* buf, int lane,
                                             const FftTables& tb) {
-#pragma unroll
-  for (int m = 0; m < 32; ++m) x[m] = cmul(x[m], ld_tw(&tb.twf[m]));
-  dft32_dif(x);
+  crt_dft32<32, CB>(x);
 #pragma unroll
   for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], ld_tw(&tb.wf[r * 32 + lane]));
   warp_transpose(x, buf, lane);
-  dft32_dif(x);
+  crt_dft32<0, CB>(x);
 }
 
-// Inverse negacyclic FFT back to folded coefficients scaled by 1/M.
+// Inverse transform back to folded coefficients scaled by 1/M.
+template <bool CB = true>
 __device__ __forceinline__ void fft_inverse(double2 (&x)[FFT_R], double2* buf, int lane,
                                             const FftTables& tb) {
-  idft32_dit(x);
+  dit_dft32<CB>(x);
 #pragma unroll
   for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], ld_tw(&tb.wi[n * 32 + lane]));
   warp_transpose(x, buf, lane);
-  idft32_dit(x);
+  dit_dft32<CB>(x);
+  untwist<10, CB>(x);
+}
+
+// The same pair through the 8 KB half buffer, the twiddles read from global memory.
+template <bool CB = true>
+__device__ __forceinline__ void fft_forward_h(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wf_g) {
+  crt_dft32<32, CB>(x);
 #pragma unroll
-  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], ld_tw(&tb.twi[n]));
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], __ldg(&wf_g[r * 32 + lane]));
+  warp_transpose_half(x, buf, lane);
+  crt_dft32<0, CB>(x);
+}
+
+template <bool CB = true>
+__device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wi_g) {
+  dit_dft32<CB>(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&wi_g[n * 32 + lane]));
+  warp_transpose_half(x, buf, lane);
+  dit_dft32<CB>(x);
+  untwist<10, CB>(x);
+}
+
+// Twiddle table T held once in shared memory for both directions.  Element (a, b) of the 32x32
+// table lives at a*32 + ((a+b) & 31): the forward transform reads row r across the lanes and
+// the inverse reads the transpose (its twiddle at lane l, register n is conj(T(l, n))); with
+// this swizzle both patterns are bank-conflict free.
+__device__ __forceinline__ int tw_swz(int a, int b) { return a * 32 + ((a + b) & 31); }
+
+template <bool CB = true>
+__device__ __forceinline__ void fft_forward_s(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wf_sw) {
+  crt_dft32<32, CB>(x);
+#pragma unroll
+  for (int r = 0; r < 32; ++r) x[r] = cmul(x[r], wf_sw[tw_swz(r, lane)]);
+  warp_transpose_half(x, buf, lane);
+  crt_dft32<0, CB>(x);
+}
+
+// Inverse scaled by 2^-SHIFT overall (SHIFT >= 10 includes the 1/M).
+template <int SHIFT, bool CB = true>
+__device__ __forceinline__ void fft_inverse_s(double2 (&x)[FFT_R], double* buf, int lane,
+                                              const double2* wf_sw) {
+  dit_dft32<CB>(x);
+#pragma unroll
+  for (int n = 0; n < 32; ++n) x[n] = cmul_conj(x[n], wf_sw[tw_swz(lane, n)]);
+  warp_transpose_half(x, buf, lane);
+  dit_dft32<CB>(x);
+  untwist<SHIFT, CB>(x);
 }
 
 // Host: build (once per device) and fetch the tables of the current device.

@@ -56,38 +56,27 @@ int fft_tables_get(FftTables* out) {
   }
   std::lock_guard<std::mutex> lk(g_tab_mu);
   if (!g_tab_ok[dev]) {
-    const int N = FFT_N, M = FFT_M;
+    const int M = FFT_M;
     const long double PI = 3.141592653589793238462643383279502884L;
-    std::vector<double2> wf(M), wi(M), twf(32), twi(32);
-    auto expi = [&](long double ang) {
+    std::vector<double2> wf(M), wi(M);
+    // T(r, l) = rho_r^l, rho_r = exp(i pi (1 + 4 bitrev(r)) / 2048): angle pi e / 2048 with the
+    // exponent reduced mod 4096 in integers first.
+    auto T = [&](int r, int l) {
+      const long long e = ((long long)l * (1 + 4 * bitrev5(r))) % 4096;
+      const long double ang = PI * (long double)e / 2048.0L;
       return make_double2((double)cosl(ang), (double)sinl(ang));
     };
     for (int r = 0; r < 32; ++r)
       for (int l = 0; l < 32; ++l) {
-        // zeta^l W^{l k2}, k2 = bitrev(r): angle pi l / N - 2 pi (l k2 mod M) / M
-        long long e = ((long long)l * bitrev5(r)) % M;
-        wf[r * 32 + l] = expi(PI * l / N - 2.0L * PI * e / M);
+        wf[r * 32 + l] = T(r, l);
+        const double2 t = T(l, r);
+        wi[r * 32 + l] = make_double2(t.x, -t.y);
       }
-    for (int n = 0; n < 32; ++n)
-      for (int l = 0; l < 32; ++l) {
-        // zeta^{-n} W^{-n k2}, k2 = bitrev(l)
-        long long e = ((long long)n * bitrev5(l)) % M;
-        wi[n * 32 + l] = expi(-PI * n / N + 2.0L * PI * e / M);
-      }
-    for (int m = 0; m < 32; ++m) {
-      twf[m] = expi(PI * (32.0L * m) / N);
-      double2 t = expi(-PI * (32.0L * m) / N);
-      twi[m] = make_double2(t.x / M, t.y / M);
-    }
     FftTables t{};
     PNB_CUDA(cudaMalloc(&t.wf, sizeof(double2) * M));
     PNB_CUDA(cudaMalloc(&t.wi, sizeof(double2) * M));
-    PNB_CUDA(cudaMalloc(&t.twf, sizeof(double2) * 32));
-    PNB_CUDA(cudaMalloc(&t.twi, sizeof(double2) * 32));
     PNB_CUDA(cudaMemcpy(t.wf, wf.data(), sizeof(double2) * M, cudaMemcpyHostToDevice));
     PNB_CUDA(cudaMemcpy(t.wi, wi.data(), sizeof(double2) * M, cudaMemcpyHostToDevice));
-    PNB_CUDA(cudaMemcpy(t.twf, twf.data(), sizeof(double2) * 32, cudaMemcpyHostToDevice));
-    PNB_CUDA(cudaMemcpy(t.twi, twi.data(), sizeof(double2) * 32, cudaMemcpyHostToDevice));
     g_tab[dev] = t;
     g_tab_ok[dev] = true;
   }
@@ -195,6 +184,15 @@ int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int c
 // ------------------------------------------------------------------------------------------
 constexpr int BR_MAXN = 1024;  // maximum small LWE dimension supported by the smem layout
 
+// Where the rotation kernels' FFT constants live (1: constant bank, 0: literals); chosen per
+// kernel by register pressure.
+#ifndef PNB_BR_CBANK
+#define PNB_BR_CBANK 1
+#endif
+#ifndef PNB_ML_CBANK
+#define PNB_ML_CBANK 0
+#endif
+
 template <int CPB>
 struct BrLayout {
   static constexpr int WARPS = 2 * CPB;
@@ -205,23 +203,23 @@ struct BrLayout {
   static constexpr int OFF_ACC = WARPS * SCRATCH;
   static constexpr int OFF_BSK = OFF_ACC + WARPS * ACC;
   static constexpr int OFF_WF = OFF_BSK + BSK;  // 16 KB twiddles (both directions, swizzled)
-  static constexpr int OFF_TWF = OFF_WF + FFT_M * (int)sizeof(double2);
-  static constexpr int OFF_TWI = OFF_TWF + 32 * (int)sizeof(double2);
-  static constexpr int OFF_ABAR = OFF_TWI + 32 * (int)sizeof(double2);
+  static constexpr int OFF_ABAR = OFF_WF + FFT_M * (int)sizeof(double2);
   static constexpr int OFF_BAR = OFF_ABAR + CPB * ABAR;
   static constexpr int BYTES = OFF_BAR + 16;
 };
 
-// The blind rotation's inverse FFT leaves v * 2^-32, v the integer nearest the exact product
-// coefficient (|v| < 2^100).  Return round(v / 2^32) mod 2^32 -- the top word of the torus
-// value -- with four FP64 operations and no integer work: w = v 2^-32 reduced by the nearest
-// multiple of 2^32 is exact (|t| <= 2^31), and adding 1.5 * 2^52 rounds t into the low
-// mantissa word.
+// The blind rotation's inverse FFT leaves w = v * 2^-32, v the exact product coefficient
+// (|v| < 2^100).  Return round(w) mod 2^32 -- the top word of the torus value -- with three FP64
+// operations and no integer work.  With C = 1.5 * 2^52: u = RN(w 2^-32 + C) = C + k,
+// k = round(w / 2^32); q = C (1 + 2^32) - 2^32 u = C - 2^32 k exactly (a multiple of 2^32 below
+// 2^72); w + q = (w - 2^32 k) + C with |w - 2^32 k| <= 2^31, so its rounding to the unit grid of
+// [2^52, 2^53) is C + round(w - 2^32 k), whose low word is round(w) mod 2^32 (C = 0 mod 2^32).
 __device__ __forceinline__ uint32_t scaled_f64_to_top32(double w) {
-  const double magic = 6755399441055744.0;  // 1.5 * 2^52
-  const double k = fma(w, 0x1p-32, magic) - magic;
-  const double t = fma(-4294967296.0, k, w);
-  return (uint32_t)__double2loint(t + magic);
+  const double magic = 6755399441055744.0;            // 1.5 * 2^52
+  const double magic_hi = 6755399441055744.0 * 4294967297.0;  // C (1 + 2^32), exact
+  const double u = fma(w, 0x1p-32, magic);
+  const double q = fma(u, -4294967296.0, magic_hi);
+  return (uint32_t)__double2loint(w + q);
 }
 
 // Named barrier over the two warps of one ciphertext.
@@ -262,8 +260,6 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   uint32_t* acc = reinterpret_cast<uint32_t*>(br_raw + L::OFF_ACC) + warp * FFT_N;
   const double2* bsk_s = reinterpret_cast<const double2*>(br_raw + L::OFF_BSK);
   double2* wf_s = reinterpret_cast<double2*>(br_raw + L::OFF_WF);
-  double2* twf_s = reinterpret_cast<double2*>(br_raw + L::OFF_TWF);
-  double2* twi_s = reinterpret_cast<double2*>(br_raw + L::OFF_TWI);
   uint16_t* abar = reinterpret_cast<uint16_t*>(br_raw + L::OFF_ABAR) + cl * BR_MAXN;
   const uint32_t bar = tc::smem_u32(br_raw + L::OFF_BAR);
   volatile int* abort_s = reinterpret_cast<volatile int*>(br_raw + L::OFF_BAR + 8);
@@ -275,11 +271,6 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     *abort_s = 0;
   }
   for (int e = threadIdx.x; e < FFT_M; e += 64 * CPB) wf_s[tw_swz(e >> 5, e & 31)] = tb.wf[e];
-  if (threadIdx.x < 32) {
-    twf_s[threadIdx.x] = tb.twf[threadIdx.x];
-    const double2 t = tb.twi[threadIdx.x];
-    twi_s[threadIdx.x] = make_double2(t.x * 0x1p-32, t.y * 0x1p-32);  // exact scaling
-  }
   __syncthreads();
   if (threadIdx.x == 0) br_stage_ggsw(bsk_dst, fbsk, bar);
 
@@ -318,7 +309,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
       const int d1 = (int)(v1 + rnd) >> shift;
       x[m] = make_double2((double)d0, (double)d1);
     }
-    fft_forward_s(x, buf, lane, wf_s, twf_s);
+    fft_forward_s<PNB_BR_CBANK>(x, buf, lane, wf_s);
     // GGSW i must have landed in shared memory (bounded wait; parity = i mod 2).
     if (!tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT)) {
       *abort_s = 1;
@@ -350,7 +341,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
     }
-    fft_inverse_s(x, buf, lane, wf_s, twi_s);
+    fft_inverse_s<10 + 32, PNB_BR_CBANK>(x, buf, lane, wf_s);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
@@ -389,7 +380,6 @@ constexpr int BR_CPB = 4;
 struct BrMlSmem {
   uint64_t acc[2][FFT_N];    // 32 KB accumulator (mask, body)
   double scratch[2][FFT_M];  // 16 KB transpose / exchange halves, one per warp
-  double2 twf[32], twi[32];
   uint16_t abar[BR_MAXN];
   uint32_t tmem_holder;
 };
@@ -434,10 +424,6 @@ __global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
   constexpr int LG = 12;
   for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
   if (warp == 0) tc::tmem_alloc(tc::smem_u32(&S.tmem_holder), 128);
-  if (threadIdx.x < 32) {
-    S.twf[threadIdx.x] = tb.twf[threadIdx.x];
-    S.twi[threadIdx.x] = tb.twi[threadIdx.x];
-  }
   const int bt = modswitch(in[n], LG);
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
   for (int t = threadIdx.x; t < FFT_N; t += 64) {
@@ -481,7 +467,7 @@ __global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
         x[m] = make_double2((double)ml_digit<L, BETA>(v0, base_log, lev),
                             (double)ml_digit<L, BETA>(v1, base_log, lev));
       }
-      fft_forward_h(x, buf, lane, tb.wf, S.twf);
+      fft_forward_h<PNB_ML_CBANK>(x, buf, lane, tb.wf);
       const double2* f_own = ggsw + ((size_t)(p * L + lev) * 2 + p) * FFT_M;
       const double2* f_oth = ggsw + ((size_t)((p ^ 1) * L + lev) * 2 + p) * FFT_M;
       const bool last = lev == L - 1;
@@ -526,7 +512,7 @@ __global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
       }
       if (!last) tc::tmem_st_wait();
     }
-    fft_inverse_h(x, buf0, lane, wi_g, S.twi);
+    fft_inverse_h<PNB_ML_CBANK>(x, buf0, lane, wi_g);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
