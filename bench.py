@@ -265,6 +265,46 @@ def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 6
     return out
 
 
+def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6)), B=4096):
+    """PBS/s of the multi-level key sets the graph planner uses (keyswitch + blind rotation,
+    device-timed at batch B, L2 flushed between repetitions), each checked by decryption."""
+    import numpy as np
+    import torch
+    rng = np.random.default_rng(SEED + 31)
+    stream = torch.cuda.current_stream(dev)
+    out = []
+    for base_log, levels in sets:
+        p = pnb.default_params()
+        p.pbs_base_log, p.pbs_level = base_log, levels
+        keys = pnb.keygen(p, seed=SEED, device=dev.index)
+        lut = rng.integers(0, 16, 16)
+        msgs = rng.integers(0, 16, B)
+        tv = pnb.test_vector(keys, lut)
+        ct = pnb.encrypt(keys, torch.tensor(msgs), seed=SEED + 32)
+        small = torch.empty((B, keys.params.n + 1), dtype=torch.int64, device=dev)
+        ks_ws = torch.empty(pnb.keyswitch_workspace_bytes(keys, B), dtype=torch.uint8, device=dev)
+        o = torch.empty_like(ct)
+        pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+        pnb.blind_rotate(keys, tv, small, out=o)
+        ok = bool(np.array_equal(pnb.decrypt_vec(keys, o).cpu().numpy(), lut[msgs]))
+        reps, ms = 3, 0.0
+        for _ in range(reps):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+            pnb.blind_rotate(keys, tv, small, out=o)
+            b.record(stream)
+            torch.cuda.synchronize(dev)
+            ms += a.elapsed_time(b)
+        ms /= reps
+        out.append({"base_log": base_log, "levels": levels, "batch": B,
+                    "pbs_per_second": B / (ms * 1e-3), "decrypt_ok": ok})
+        del ct, small, ks_ws, o
+        keys.free()
+    return out
+
+
 def noise_leg(pnb, keys, dev, total=100352):
     """Output noise of the single-level bootstrap over ~1e5 bootstraps (phase - LUT*delta)."""
     import numpy as np
@@ -532,6 +572,7 @@ def run_gpu(args):
                                                                            flush)
     noise = noise_leg(pnb, keys, dev) if (rank == 0 and args.noise) else None
     sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
+    key_sets = key_set_leg(pnb, dev, flush) if (rank == 0 and args.key_sets) else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -563,6 +604,7 @@ def run_gpu(args):
             "contraction": contraction,
             "noise": noise,
             "pbs_batch_sweep": sweep,
+            "pbs_by_key_set": key_sets,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -584,6 +626,8 @@ def main():
                     help="samples of the Linear 784->128 contraction leg (0 skips it)")
     ap.add_argument("--sweep", type=int, default=1,
                     help="PBS/s across batch sizes 1..65536 (rank 0)")
+    ap.add_argument("--key-sets", type=int, default=1,
+                    help="PBS/s of the multi-level key sets at batch 4096 (rank 0)")
     ap.add_argument("--noise", type=int, default=1,
                     help="measure the bootstrap output noise over ~1e5 bootstraps (rank 0)")
     ap.add_argument("--mlp-batch", type=int, default=32,

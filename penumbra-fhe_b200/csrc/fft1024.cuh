@@ -137,12 +137,12 @@ __device__ __forceinline__ void dit_dft32(double2 (&x)[FFT_R]) {
   dit_stage<5, CB>(x);
 }
 
-// x_m *= exp(-2 pi i m / 128) * 2^-SHIFT, SHIFT = 10 (the 1/M) or 42 (also the 2^-32 the blind
-// rotation's rounding expects); the constants come pre-scaled.
+// x_m *= exp(-2 pi i m / 128) * 2^-SHIFT, SHIFT = 10 (the 1/M), 26 or 42 (also the 2^-16 or
+// 2^-32 a blind rotation's rounding expects); the constants come pre-scaled.
 template <int SHIFT, bool CB>
 __device__ __forceinline__ void untwist(double2 (&x)[FFT_R]) {
-  static_assert(SHIFT == 10 || SHIFT == 42, "untwist tables exist for 2^-10 and 2^-42");
-  const double2* k = SHIFT == 10 ? kUntwist10 : kUntwist42;
+  static_assert(SHIFT == 10 || SHIFT == 26 || SHIFT == 42, "no untwist table for this scale");
+  const double2* k = SHIFT == 10 ? kUntwist10 : SHIFT == 26 ? kUntwist26 : kUntwist42;
   constexpr double sc = 1.0 / (double)(1ull << SHIFT);
 #pragma unroll
   for (int m = 0; m < 32; ++m) {
@@ -228,7 +228,7 @@ __device__ __forceinline__ void fft_forward_h(double2 (&x)[FFT_R], double* buf, 
   crt_dft32<0, CB>(x);
 }
 
-template <bool CB = true>
+template <bool CB = true, int SHIFT = 10>
 __device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, int lane,
                                               const double2* wi_g) {
   dit_dft32<CB>(x);
@@ -236,7 +236,7 @@ __device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, 
   for (int n = 0; n < 32; ++n) x[n] = cmul(x[n], __ldg(&wi_g[n * 32 + lane]));
   warp_transpose_half(x, buf, lane);
   dit_dft32<CB>(x);
-  untwist<10, CB>(x);
+  untwist<SHIFT, CB>(x);
 }
 
 // Twiddle table T held once in shared memory for both directions.  Element (a, b) of the 32x32

@@ -190,7 +190,7 @@ constexpr int BR_MAXN = 1024;  // maximum small LWE dimension supported by the s
 #define PNB_BR_CBANK 1
 #endif
 #ifndef PNB_ML_CBANK
-#define PNB_ML_CBANK 0
+#define PNB_ML_CBANK 1
 #endif
 
 template <int CPB>
@@ -367,23 +367,6 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 
 constexpr int BR_CPB = 4;
 
-// ------------------------------------------------------------------------------------------
-// Multi-level blind rotation (pbs_level 2..6, the low-noise key sets).  One ciphertext per
-// 64-thread block, warp p owning accumulator polynomial p (u64 words: the gadget digits need
-// base_log * level > 32 bits of it).  Per CMux and level the warp forms its digit polynomial,
-// transforms it, exchanges the spectrum with the other warp in two 8 KB halves and accumulates
-// D_own * F[own row][p] + D_other * F[other row][p].  The sums of levels 0..L-2 live in tensor
-// memory (128 columns per block: warp p uses lanes 32p..32p+31, four columns per spectrum row),
-// the last level's in registers, which then go through the inverse transform.  Shared memory
-// holds only the accumulator, the scratch halves and the ciphertext's rotation amounts (about
-// 51 KB), so four blocks (eight warps) run per SM; the forward twiddles come through L1.
-struct BrMlSmem {
-  uint64_t acc[2][FFT_N];    // 32 KB accumulator (mask, body)
-  double scratch[2][FFT_M];  // 16 KB transpose / exchange halves, one per warp
-  uint16_t abar[BR_MAXN];
-  uint32_t tmem_holder;
-};
-
 // Balanced base-2^beta digit `lev` (0 = most significant) of the top beta*L bits of v, rounded:
 // the balanced digits of st are the plain digits of st + sum_j 2^(beta-1) 2^(beta j), each
 // minus 2^(beta-1) (the top carry falls off mod 2^(beta L), as it does on the torus).  BETA > 0
@@ -401,81 +384,143 @@ __device__ __forceinline__ int ml_digit(uint64_t v, int beta_rt, int lev) {
   return (int)(u & ((1ull << beta) - 1)) - (int)half;
 }
 
-// Streaming read of the bootstrapping key: no L1 allocation, so the key stream (32 KB per
-// warp and level) does not evict the lines that hold the kernel's register spills.
-__device__ __forceinline__ double2 ld_key_stream(const double2* p) {
-  double2 v;
-  asm("ld.global.nc.L1::no_allocate.v2.f64 {%0, %1}, [%2];" : "=d"(v.x), "=d"(v.y) : "l"(p));
-  return v;
+// ------------------------------------------------------------------------------------------
+// Blocked multi-level blind rotation (pbs_level 2..6).  A block bootstraps MLB_CPB ciphertexts
+// in lockstep, warp (2c + p) owning accumulator polynomial p of ciphertext c, like the single-
+// level kernel; per CMux it walks the gadget levels, and each level's part of the GGSW (the mask
+// and body rows of that level, 64 KB) is staged once per block in shared memory by bulk copy
+// while the warps form and transform the level's digits, so the ciphertexts of a block share
+// every key byte.  The sums of levels 0..L-2 live in tensor memory (128 columns per warp: warps
+// w and w + 4 share a lane quarter), the last level's in registers, which then go through the
+// inverse transform.  The accumulator keeps the top 48 bits of each torus coefficient (u64
+// words whose low 16 bits stay zero): the gadget digits read at most 42 bits plus a rounding
+// bit, and the dropped bits (< 2^16 per CMux) stay far below the f64 product's own error.
+// ------------------------------------------------------------------------------------------
+constexpr int MLB_CPB = 3;
+
+struct MlbLayout {
+  static constexpr int WARPS = 2 * MLB_CPB;
+  static constexpr int SCRATCH = FFT_M * sizeof(double);      // 8 KB per warp
+  static constexpr int ACC = FFT_N * sizeof(uint64_t);        // 16 KB per warp
+  static constexpr int GGSW = 4 * FFT_M * sizeof(double2);    // 64 KB: one level
+  static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);     // 2 KB per ciphertext
+  static constexpr int OFF_ACC = WARPS * SCRATCH;
+  static constexpr int OFF_GGSW = OFF_ACC + WARPS * ACC;
+  static constexpr int OFF_ABAR = OFF_GGSW + GGSW;
+  static constexpr int OFF_BAR = OFF_ABAR + MLB_CPB * ABAR;  // mbarrier, abort flag, TMEM base
+  static constexpr int BYTES = OFF_BAR + 16;
+  static constexpr int TMEM_COLS = 256;
+};
+
+// w = v 2^-16 for the exact product coefficient v (|w| < 2^86).  Returns round(w) mod 2^48 in the
+// top 48 bits of a torus word, with three FP64 operations: with C = 1.5 * 2^52,
+// u = RN(w 2^-48 + C) = C + k, k = round(w / 2^48); q = C (1 + 2^48) - 2^48 u = C - 2^48 k
+// exactly; w + q = (w - 2^48 k) + C with |w - 2^48 k| <= 2^47, so its rounding to the unit grid of
+// [2^52, 2^53) is C + round(w - 2^48 k), and the low 48 bits of that double's encoding are
+// round(w) mod 2^48 (C's mantissa 2^51 is 0 mod 2^48).
+__device__ __forceinline__ uint64_t scaled_f64_to_top48(double w) {
+  const double magic = 6755399441055744.0;                    // 1.5 * 2^52
+  const double magic_hi = 6755399441055744.0 * 281474976710657.0;  // C (1 + 2^48), exact
+  const double u = fma(w, 0x1p-48, magic);
+  const double q = fma(u, -281474976710656.0, magic_hi);
+  return (uint64_t)__double_as_longlong(w + q) << 16;
+}
+
+// Stage level `lev` of GGSW `i` (key set with L levels): the mask row's two polynomials to slots
+// 0..1 and the body row's to slots 2..3 (64 KB).
+template <int L>
+__device__ __forceinline__ void mlb_stage(uint32_t dst, const double2* fbsk, int i, int lev,
+                                          uint32_t bar) {
+  const double2* g = fbsk + (size_t)i * (2 * L) * 2 * FFT_M;
+  tc::mbar_expect_tx(bar, 4 * FFT_M * sizeof(double2));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int row = (q < 2 ? 0 : L) + lev;
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+        ::"r"(dst + q * FFT_M * 16u), "l"(g + (size_t)(row * 2 + (q & 1)) * FFT_M),
+        "r"(FFT_M * 16u), "r"(bar)
+        : "memory");
+  }
 }
 
 template <int L, int BETA>
-__global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
-    const uint64_t* __restrict__ small_ct, TvSel sel,
-    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
-    int base_log, FftTables tb) {
-  extern __shared__ __align__(16) unsigned char ml_raw[];
-  BrMlSmem& S = *reinterpret_cast<BrMlSmem*>(ml_raw);
+__global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
+    const uint64_t* __restrict__ small_ct, TvSel sel, const double2* __restrict__ fbsk,
+    uint64_t* __restrict__ out, int count, int n, int base_log, FftTables tb) {
+  using Y = MlbLayout;
+  extern __shared__ __align__(128) unsigned char mlb_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int p = warp;
-  const int ct = blockIdx.x;
-  const uint64_t* in = small_ct + (size_t)ct * (n + 1);
-  const uint64_t* tv = tv_of(sel, ct);
-  constexpr int LG = 12;
-  for (int i = threadIdx.x; i < n; i += 64) S.abar[i] = (uint16_t)modswitch(in[i], LG);
-  if (warp == 0) tc::tmem_alloc(tc::smem_u32(&S.tmem_holder), 128);
-  const int bt = modswitch(in[n], LG);
-  const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = threadIdx.x; t < FFT_N; t += 64) {
-    S.acc[0][t] = 0;
-    S.acc[1][t] = rot_coef(tv, t, r0);
+  const int cl = warp >> 1, p = warp & 1;
+  const int ct = blockIdx.x * MLB_CPB + cl;
+  const bool valid = ct < count;
+  constexpr int LG = 12;  // log2(2N)
+  double* buf = reinterpret_cast<double*>(mlb_raw) + warp * FFT_M;
+  double2* xch = reinterpret_cast<double2*>(buf);
+  const double2* och = reinterpret_cast<const double2*>(reinterpret_cast<double*>(mlb_raw) +
+                                                        (warp ^ 1) * FFT_M);
+  uint64_t* acc = reinterpret_cast<uint64_t*>(mlb_raw + Y::OFF_ACC) + warp * FFT_N;
+  const double2* ggsw_s = reinterpret_cast<const double2*>(mlb_raw + Y::OFF_GGSW);
+  uint16_t* abar = reinterpret_cast<uint16_t*>(mlb_raw + Y::OFF_ABAR) + cl * BR_MAXN;
+  const uint32_t bar = tc::smem_u32(mlb_raw + Y::OFF_BAR);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(mlb_raw + Y::OFF_BAR + 8);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mlb_raw + Y::OFF_BAR + 12);
+  const uint32_t ggsw_dst = tc::smem_u32(mlb_raw + Y::OFF_GGSW);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+    *abort_s = 0;
   }
+  if (warp == 0) tc::tmem_alloc(tc::smem_u32(tmem_holder), Y::TMEM_COLS);
   tc::tc_fence_before();
   __syncthreads();
   tc::tc_fence_after();
-  // this warp's lane quarter; column 4r + {0..3} holds the double2 of spectrum row r
-  const uint32_t tfacc = *reinterpret_cast<volatile uint32_t*>(&S.tmem_holder) +
-                         ((uint32_t)(32 * p) << 16);
-  uint64_t* my0 = S.acc[p];
-  double* buf0 = S.scratch[p];
-  double2* xch0 = reinterpret_cast<double2*>(S.scratch[p]);
-  const double2* och0 = reinterpret_cast<const double2*>(S.scratch[p ^ 1]);
-  const double2* wi_g = tb.wi;
+  if (threadIdx.x == 0) mlb_stage<L>(ggsw_dst, fbsk, 0, 0, bar);
 
-  for (int i = 0; i < n; ++i) {
-    const int a = S.abar[i];
-    if (a == 0) continue;  // X^0 - 1 = 0: the CMux leaves the accumulator unchanged
+  const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
+  const uint64_t* tv = tv_of(sel, valid ? ct : 0);
+  const int t64 = threadIdx.x & 63;
+  for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
+  const int bt = valid ? modswitch(in[n], LG) : 0;
+  const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
+  for (int t = lane; t < FFT_N; t += 32) acc[t] = (p == 0) ? 0 : rot_coef(tv, t, r0);
+  __syncthreads();
 
-    const double2* ggsw = fbsk + (size_t)i * (2 * L) * 2 * FFT_M;
+  // this warp's lane quarter and column range; column 4r + {0..3} holds spectrum row r
+  const uint32_t tfacc = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
+                         ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
+  const double2* f_own = ggsw_s + (size_t)(p * 2 + p) * FFT_M;
+  const double2* f_oth = ggsw_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
+  uint32_t stage = 0;
+  bool aborted = false;
+
+  for (int i = 0; i < n && !aborted; ++i) {
+    const int a = abar[i];
     double2 x[FFT_R];
 #pragma unroll 1
     for (int lev = 0; lev < L; ++lev) {
-      // Opaque per-level copies of the shared-memory pointers (three levels and more): every
-      // address below is loop invariant, and hoisting all of them out of the level loop spills
-      // registers.
-      uint64_t* my = my0;
-      double* buf = buf0;
-      double2* xch = xch0;
-      const double2* och = och0;
-      if (L > 2) asm volatile("" : "+l"(my), "+l"(buf), "+l"(xch), "+l"(och));
 #pragma unroll
       for (int m = 0; m < 32; ++m) {
         if ((m & 7) == 0) asm volatile("" ::: "memory");
         const int j = lane + 32 * m;
-        const uint64_t v0 = rot_coef(my, j, a) - my[j];
-        const uint64_t v1 = rot_coef(my, j + FFT_M, a) - my[j + FFT_M];
+        const uint64_t v0 = rot_coef(acc, j, a) - acc[j];
+        const uint64_t v1 = rot_coef(acc, j + FFT_M, a) - acc[j + FFT_M];
         x[m] = make_double2((double)ml_digit<L, BETA>(v0, base_log, lev),
                             (double)ml_digit<L, BETA>(v1, base_log, lev));
       }
       fft_forward_h<PNB_ML_CBANK>(x, buf, lane, tb.wf);
-      const double2* f_own = ggsw + ((size_t)(p * L + lev) * 2 + p) * FFT_M;
-      const double2* f_oth = ggsw + ((size_t)((p ^ 1) * L + lev) * 2 + p) * FFT_M;
+      // this level's key rows must have landed (bounded wait; parity = stage mod 2)
+      if (!tc::mbar_wait(bar, stage & 1u, BR_WAIT_LIMIT)) {
+        *abort_s = 1;
+        atomicExch(&g_br_status, 1);
+      }
       const bool last = lev == L - 1;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
 #pragma unroll
         for (int rr = 0; rr < 16; ++rr) xch[rr * 32 + lane] = x[16 * h + rr];
-        pair_sync(0);
+        pair_sync(cl);
 #pragma unroll
         for (int g4 = 0; g4 < 4; ++g4) {
           const int rb = 16 * h + 4 * g4;  // four spectrum rows = 16 TMEM columns
@@ -488,7 +533,7 @@ __global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
           for (int q = 0; q < 4; ++q) {
             const int r = rb + q;
             const int e = r * 32 + lane;
-            const double2 fo = ld_key_stream(&f_own[e]), ft = ld_key_stream(&f_oth[e]);
+            const double2 fo = f_own[e], ft = f_oth[e];
             const double2 dt = och[(r - 16 * h) * 32 + lane];
             const double2 p0 = cmul(x[r], fo);
             double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
@@ -508,41 +553,66 @@ __global__ void __launch_bounds__(64, 4) blind_rotate_ml_kernel(
           }
           if (!last) tc::tmem_st_32x32_x16(tfacc + (uint32_t)(4 * rb), t);
         }
-        pair_sync(0);
+        pair_sync(cl);
       }
       if (!last) tc::tmem_st_wait();
+      // every warp is done with this level's key rows: stage the next level (or the next CMux's
+      // first level) while the warps carry on
+      __syncthreads();
+      if (*abort_s) {  // uniform: read by every thread after the same barrier
+        aborted = true;
+        break;
+      }
+      ++stage;
+      if (threadIdx.x == 0 && (i + 1 < n || lev + 1 < L)) {
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        if (lev + 1 < L) mlb_stage<L>(ggsw_dst, fbsk, i, lev + 1, bar);
+        else mlb_stage<L>(ggsw_dst, fbsk, i + 1, 0, bar);
+      }
     }
-    fft_inverse_h<PNB_ML_CBANK>(x, buf0, lane, wi_g);
+    if (aborted) break;
+    fft_inverse_h<PNB_ML_CBANK, 10 + 16>(x, buf, lane, tb.wi);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      my0[j] += f64_to_torus(x[m].x);
-      my0[j + FFT_M] += f64_to_torus(x[m].y);
+      acc[j] += scaled_f64_to_top48(x[m].x);
+      acc[j + FFT_M] += scaled_f64_to_top48(x[m].y);
     }
     __syncwarp();
+  }
+  if (aborted && threadIdx.x == 0) {
+    // a copy of the stage that timed out may still be in flight: let it land (bounded) before
+    // the block's shared memory is released
+    (void)tc::mbar_wait(bar, stage & 1u, BR_WAIT_LIMIT);
   }
   tc::tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(&S.tmem_holder), 128);
+    tc::tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(tmem_holder), Y::TMEM_COLS);
   }
-  uint64_t* o = out + (size_t)ct * (FFT_N + 1);
-  for (int t = threadIdx.x; t < FFT_N; t += 64)
-    o[t] = (t == 0) ? S.acc[0][0] : (uint64_t)0 - S.acc[0][FFT_N - t];
-  if (threadIdx.x == 0) o[FFT_N] = S.acc[1][0];
+  // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
+  if (valid && !aborted) {
+    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    if (p == 0) {
+      for (int t = lane; t < FFT_N; t += 32) o[t] = (t == 0) ? acc[0] : (uint64_t)0 - acc[FFT_N - t];
+    } else if (lane == 0) {
+      o[FFT_N] = acc[0];
+    }
+  }
 }
 
 template <int L, int BETA>
-static int launch_ml(const pnb_keys* K, TvSel tv, const uint64_t* small,
-                     uint64_t* out, int count, FftTables tb, cudaStream_t st) {
-  const int smem = sizeof(BrMlSmem);
-  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_ml_kernel<L, BETA>,
+static int launch_mlb(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64_t* out,
+                      int count, FftTables tb, cudaStream_t st) {
+  constexpr int smem = MlbLayout::BYTES;
+  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_mlb_kernel<L, BETA>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  blind_rotate_ml_kernel<L, BETA><<<count, 64, smem, st>>>(small, tv, K->fbsk, out, count,
-                                                           K->p.n, K->p.pbs_base_log, tb);
-  PNB_CHECK_LAUNCH("blind_rotate_ml_kernel");
+  const int blocks = (count + MLB_CPB - 1) / MLB_CPB;
+  blind_rotate_mlb_kernel<L, BETA><<<blocks, 64 * MLB_CPB, smem, st>>>(
+      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+  PNB_CHECK_LAUNCH("blind_rotate_mlb_kernel");
   return PNB_OK;
 }
 
@@ -550,9 +620,9 @@ static int launch_ml(const pnb_keys* K, TvSel tv, const uint64_t* small,
 template <int L, int B0, int B1 = 0>
 static int launch_ml_any(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64_t* out,
                          int count, FftTables tb, cudaStream_t st) {
-  if (B0 > 0 && K->p.pbs_base_log == B0) return launch_ml<L, B0>(K, tv, small, out, count, tb, st);
-  if (B1 > 0 && K->p.pbs_base_log == B1) return launch_ml<L, B1>(K, tv, small, out, count, tb, st);
-  return launch_ml<L, 0>(K, tv, small, out, count, tb, st);
+  if (B0 > 0 && K->p.pbs_base_log == B0) return launch_mlb<L, B0>(K, tv, small, out, count, tb, st);
+  if (B1 > 0 && K->p.pbs_base_log == B1) return launch_mlb<L, B1>(K, tv, small, out, count, tb, st);
+  return launch_mlb<L, 0>(K, tv, small, out, count, tb, st);
 }
 
 static bool br_supported(const pnb_params& p) {
