@@ -367,32 +367,17 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 
 constexpr int BR_CPB = 4;
 
-// Balanced base-2^beta digit `lev` (0 = most significant) of the top beta*L bits of v, rounded:
-// the balanced digits of st are the plain digits of st + sum_j 2^(beta-1) 2^(beta j), each
-// minus 2^(beta-1) (the top carry falls off mod 2^(beta L), as it does on the torus).  BETA > 0
-// makes every constant a compile-time value; BETA = 0 takes beta at run time.
-template <int L, int BETA>
-__device__ __forceinline__ int ml_digit(uint64_t v, int beta_rt, int lev) {
-  const int beta = BETA > 0 ? BETA : beta_rt;
-  const int total = beta * L;
-  const uint64_t st = (v >> (64 - total)) + ((v >> (63 - total)) & 1u);
-  const uint64_t half = 1ull << (beta - 1);
-  uint64_t H = 0;
-#pragma unroll
-  for (int j = 0; j < L; ++j) H |= half << (beta * j);
-  const uint64_t u = (st + H) >> (beta * (L - 1 - lev));
-  return (int)(u & ((1ull << beta) - 1)) - (int)half;
-}
-
 // ------------------------------------------------------------------------------------------
 // Blocked multi-level blind rotation (pbs_level 2..6).  A block bootstraps MLB_CPB ciphertexts
 // in lockstep, warp (2c + p) owning accumulator polynomial p of ciphertext c, like the single-
 // level kernel; per CMux it walks the gadget levels, and each level's part of the GGSW (the mask
 // and body rows of that level, 64 KB) is staged once per block in shared memory by bulk copy
 // while the warps form and transform the level's digits, so the ciphertexts of a block share
-// every key byte.  The sums of levels 0..L-2 live in tensor memory (128 columns per warp: warps
-// w and w + 4 share a lane quarter), the last level's in registers, which then go through the
-// inverse transform.  The accumulator keeps the top 48 bits of each torus coefficient (u64
+// every key byte.  Tensor memory holds, per warp, the sums of levels 0..L-2 (128 columns; the
+// last level's sum stays in registers and goes through the inverse transform) and the rounded,
+// offset coefficient differences the first level computes from the accumulator (128 columns),
+// from which every later level reads its digits with a shift and a mask; warps w and w + 4 share
+// a lane quarter, so the block takes all 512 columns.  The accumulator keeps the top 48 bits of each torus coefficient (u64
 // words whose low 16 bits stay zero): the gadget digits read at most 42 bits plus a rounding
 // bit, and the dropped bits (< 2^16 per CMux) stay far below the f64 product's own error.
 // ------------------------------------------------------------------------------------------
@@ -409,7 +394,7 @@ struct MlbLayout {
   static constexpr int OFF_ABAR = OFF_GGSW + GGSW;
   static constexpr int OFF_BAR = OFF_ABAR + MLB_CPB * ABAR;  // mbarrier, abort flag, TMEM base
   static constexpr int BYTES = OFF_BAR + 16;
-  static constexpr int TMEM_COLS = 256;
+  static constexpr int TMEM_COLS = 512;  // per warp: 128 level-sum + 128 digit-source columns
 };
 
 // w = v 2^-16 for the exact product coefficient v (|w| < 2^86).  Returns round(w) mod 2^48 in the
@@ -490,24 +475,70 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   // this warp's lane quarter and column range; column 4r + {0..3} holds spectrum row r
   const uint32_t tfacc = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
                          ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
+  const uint32_t tvk = tfacc + 256u;  // the level-0 pass's vk words, 128 columns further on
   const double2* f_own = ggsw_s + (size_t)(p * 2 + p) * FFT_M;
   const double2* f_oth = ggsw_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
+  // Gadget digits: with T = beta L and H = sum_j 2^(beta-1) 2^(beta j), the balanced digits of
+  // the top T bits of v, rounded, are the plain base-2^beta digits of round(v / 2^(64-T)) + H,
+  // each minus 2^(beta-1); that sum is the top T bits of vk = v + vk_off (mod 2^64) with
+  // vk_off = 2^(63-T) + H 2^(64-T), the rounding folded into the carry.
+  const int beta = BETA > 0 ? BETA : base_log;
+  uint64_t hsum = 0;
+#pragma unroll
+  for (int j = 0; j < L; ++j) hsum |= (1ull << (beta - 1)) << (beta * j);
+  const uint64_t vk_off = (1ull << (63 - beta * L)) + (hsum << (64 - beta * L));
+  const uint32_t dmask = (1u << beta) - 1u;
+  const int dhalf = 1 << (beta - 1);
   uint32_t stage = 0;
   bool aborted = false;
 
   for (int i = 0; i < n && !aborted; ++i) {
     const int a = abar[i];
     double2 x[FFT_R];
+    {
+      // vk = (X^a acc - acc) + vk_off for both halves of every coefficient pair, into tensor
+      // memory (four columns per register pair); X^a = (-1)^(a >= N) X^(a mod N): rotate by ar
+      // in [0, N) and flip the sign where the rotation wraps.
+      const int ar = a & (FFT_N - 1);
+      const uint64_t flip = (a >= FFT_N) ? ~0ull : 0ull;
+#pragma unroll
+      for (int g = 0; g < 8; ++g) {
+        uint32_t t[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int j = lane + 32 * (4 * g + q);
+          const int s0 = j - ar, s1 = j + FFT_M - ar;
+          const uint64_t n0 = (uint64_t)(int64_t)(s0 >> 31) ^ flip;
+          const uint64_t n1 = (uint64_t)(int64_t)(s1 >> 31) ^ flip;
+          const uint64_t g0 = acc[s0 & (FFT_N - 1)], g1 = acc[s1 & (FFT_N - 1)];
+          const uint64_t v0 = ((g0 ^ n0) - n0) - acc[j] + vk_off;
+          const uint64_t v1 = ((g1 ^ n1) - n1) - acc[j + FFT_M] + vk_off;
+          t[4 * q + 0] = (uint32_t)v0;
+          t[4 * q + 1] = (uint32_t)(v0 >> 32);
+          t[4 * q + 2] = (uint32_t)v1;
+          t[4 * q + 3] = (uint32_t)(v1 >> 32);
+        }
+        tc::tmem_st_32x32_x16(tvk + (uint32_t)(16 * g), t);
+      }
+      tc::tmem_st_wait();
+    }
 #pragma unroll 1
     for (int lev = 0; lev < L; ++lev) {
+      // digit `lev` sits in bits [sh, sh + beta) of vk: a funnel shift by min(sh, 32), then sh - 32
+      const int sh = 64 - beta * (lev + 1);
+      const int sh_a = sh < 32 ? sh : 32, sh_b = sh - sh_a;
 #pragma unroll
-      for (int m = 0; m < 32; ++m) {
-        if ((m & 7) == 0) asm volatile("" ::: "memory");
-        const int j = lane + 32 * m;
-        const uint64_t v0 = rot_coef(acc, j, a) - acc[j];
-        const uint64_t v1 = rot_coef(acc, j + FFT_M, a) - acc[j + FFT_M];
-        x[m] = make_double2((double)ml_digit<L, BETA>(v0, base_log, lev),
-                            (double)ml_digit<L, BETA>(v1, base_log, lev));
+      for (int g = 0; g < 8; ++g) {
+        uint32_t t[16];
+        tc::tmem_ld_32x32_x16(tvk + (uint32_t)(16 * g), t);
+        tc::tmem_ld_wait();
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int d = (int)((__funnelshift_rc(t[2 * q], t[2 * q + 1], sh_a) >> sh_b) & dmask) -
+                        dhalf;
+          if (q & 1) x[4 * g + (q >> 1)].y = (double)d;
+          else x[4 * g + (q >> 1)].x = (double)d;
+        }
       }
       fft_forward_h<PNB_ML_CBANK>(x, buf, lane, tb.wf);
       // this level's key rows must have landed (bounded wait; parity = stage mod 2)
