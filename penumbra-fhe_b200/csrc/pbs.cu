@@ -381,18 +381,18 @@ constexpr int BR_CPB = 4;
 // words whose low 16 bits stay zero): the gadget digits read at most 42 bits plus a rounding
 // bit, and the dropped bits (< 2^16 per CMux) stay far below the f64 product's own error.
 // ------------------------------------------------------------------------------------------
-constexpr int MLB_CPB = 3;
+constexpr int MLB_CPB = 4;
 
 struct MlbLayout {
   static constexpr int WARPS = 2 * MLB_CPB;
   static constexpr int SCRATCH = FFT_M * sizeof(double);      // 8 KB per warp
-  static constexpr int ACC = FFT_N * sizeof(uint64_t);        // 16 KB per warp
+  static constexpr int ACC_HI = FFT_N * sizeof(uint32_t);     // 8 KB per warp: bits 32..63
+  static constexpr int ACC_LO = FFT_N * sizeof(uint16_t);     // 4 KB per warp: bits 16..31
   static constexpr int GGSW = 4 * FFT_M * sizeof(double2);    // 64 KB: one level
-  static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);     // 2 KB per ciphertext
-  static constexpr int OFF_ACC = WARPS * SCRATCH;
-  static constexpr int OFF_GGSW = OFF_ACC + WARPS * ACC;
-  static constexpr int OFF_ABAR = OFF_GGSW + GGSW;
-  static constexpr int OFF_BAR = OFF_ABAR + MLB_CPB * ABAR;  // mbarrier, abort flag, TMEM base
+  static constexpr int OFF_HI = WARPS * SCRATCH;
+  static constexpr int OFF_LO = OFF_HI + WARPS * ACC_HI;
+  static constexpr int OFF_GGSW = OFF_LO + WARPS * ACC_LO;
+  static constexpr int OFF_BAR = OFF_GGSW + GGSW;  // mbarrier, abort flag, TMEM base
   static constexpr int BYTES = OFF_BAR + 16;
   static constexpr int TMEM_COLS = 512;  // per warp: 128 level-sum + 128 digit-source columns
 };
@@ -444,9 +444,17 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   double2* xch = reinterpret_cast<double2*>(buf);
   const double2* och = reinterpret_cast<const double2*>(reinterpret_cast<double*>(mlb_raw) +
                                                         (warp ^ 1) * FFT_M);
-  uint64_t* acc = reinterpret_cast<uint64_t*>(mlb_raw + Y::OFF_ACC) + warp * FFT_N;
+  // accumulator word t = hi[t] 2^32 + lo[t] 2^16 (the low 16 bits stay zero)
+  uint32_t* acc_hi = reinterpret_cast<uint32_t*>(mlb_raw + Y::OFF_HI) + warp * FFT_N;
+  uint16_t* acc_lo = reinterpret_cast<uint16_t*>(mlb_raw + Y::OFF_LO) + warp * FFT_N;
+  auto acc_get = [&](int t) {
+    return ((uint64_t)acc_hi[t] << 32) | ((uint64_t)acc_lo[t] << 16);
+  };
+  auto acc_put = [&](int t, uint64_t v) {
+    acc_hi[t] = (uint32_t)(v >> 32);
+    acc_lo[t] = (uint16_t)(v >> 16);
+  };
   const double2* ggsw_s = reinterpret_cast<const double2*>(mlb_raw + Y::OFF_GGSW);
-  uint16_t* abar = reinterpret_cast<uint16_t*>(mlb_raw + Y::OFF_ABAR) + cl * BR_MAXN;
   const uint32_t bar = tc::smem_u32(mlb_raw + Y::OFF_BAR);
   volatile int* abort_s = reinterpret_cast<volatile int*>(mlb_raw + Y::OFF_BAR + 8);
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(mlb_raw + Y::OFF_BAR + 12);
@@ -465,11 +473,10 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
 
   const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
   const uint64_t* tv = tv_of(sel, valid ? ct : 0);
-  const int t64 = threadIdx.x & 63;
-  for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
   const int bt = valid ? modswitch(in[n], LG) : 0;
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = lane; t < FFT_N; t += 32) acc[t] = (p == 0) ? 0 : rot_coef(tv, t, r0);
+  for (int t = lane; t < FFT_N; t += 32) acc_put(t, (p == 0) ? 0 : rot_coef(tv, t, r0));
+  uint64_t a_next = valid ? in[0] : 0;  // mask coefficient of the next CMux, loaded one ahead
   __syncthreads();
 
   // this warp's lane quarter and column range; column 4r + {0..3} holds spectrum row r
@@ -493,7 +500,8 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   bool aborted = false;
 
   for (int i = 0; i < n && !aborted; ++i) {
-    const int a = abar[i];
+    const int a = modswitch(a_next, LG);
+    if (valid && i + 1 < n) a_next = in[i + 1];
     double2 x[FFT_R];
     {
       // vk = (X^a acc - acc) + vk_off for both halves of every coefficient pair, into tensor
@@ -510,9 +518,9 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
           const int s0 = j - ar, s1 = j + FFT_M - ar;
           const uint64_t n0 = (uint64_t)(int64_t)(s0 >> 31) ^ flip;
           const uint64_t n1 = (uint64_t)(int64_t)(s1 >> 31) ^ flip;
-          const uint64_t g0 = acc[s0 & (FFT_N - 1)], g1 = acc[s1 & (FFT_N - 1)];
-          const uint64_t v0 = ((g0 ^ n0) - n0) - acc[j] + vk_off;
-          const uint64_t v1 = ((g1 ^ n1) - n1) - acc[j + FFT_M] + vk_off;
+          const uint64_t g0 = acc_get(s0 & (FFT_N - 1)), g1 = acc_get(s1 & (FFT_N - 1));
+          const uint64_t v0 = ((g0 ^ n0) - n0) - acc_get(j) + vk_off;
+          const uint64_t v1 = ((g1 ^ n1) - n1) - acc_get(j + FFT_M) + vk_off;
           t[4 * q + 0] = (uint32_t)v0;
           t[4 * q + 1] = (uint32_t)(v0 >> 32);
           t[4 * q + 2] = (uint32_t)v1;
@@ -607,8 +615,8 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      acc[j] += scaled_f64_to_top48(x[m].x);
-      acc[j + FFT_M] += scaled_f64_to_top48(x[m].y);
+      acc_put(j, acc_get(j) + scaled_f64_to_top48(x[m].x));
+      acc_put(j + FFT_M, acc_get(j + FFT_M) + scaled_f64_to_top48(x[m].y));
     }
     __syncwarp();
   }
@@ -627,9 +635,10 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   if (valid && !aborted) {
     uint64_t* o = out + (size_t)ct * (FFT_N + 1);
     if (p == 0) {
-      for (int t = lane; t < FFT_N; t += 32) o[t] = (t == 0) ? acc[0] : (uint64_t)0 - acc[FFT_N - t];
+      for (int t = lane; t < FFT_N; t += 32)
+        o[t] = (t == 0) ? acc_get(0) : (uint64_t)0 - acc_get(FFT_N - t);
     } else if (lane == 0) {
-      o[FFT_N] = acc[0];
+      o[FFT_N] = acc_get(0);
     }
   }
 }
