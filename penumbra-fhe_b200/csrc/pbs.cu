@@ -257,7 +257,9 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   double2* xbuf = reinterpret_cast<double2*>(buf);  // the same 8 KB seen as 512 complex
   const double2* obuf = reinterpret_cast<const double2*>(reinterpret_cast<double*>(br_raw) +
                                                          (warp ^ 1) * FFT_M);
-  uint32_t* acc = reinterpret_cast<uint32_t*>(br_raw + L::OFF_ACC) + warp * FFT_N;
+  // accumulator coefficients (j, j + M) side by side: acc2[j] = (acc[j], acc[j + M]), j < M
+  uint2* acc2 = reinterpret_cast<uint2*>(br_raw + L::OFF_ACC) + warp * FFT_M;
+  auto acc_at = [&](int e) { return e < FFT_M ? acc2[e].x : acc2[e - FFT_M].y; };
   const double2* bsk_s = reinterpret_cast<const double2*>(br_raw + L::OFF_BSK);
   double2* wf_s = reinterpret_cast<double2*>(br_raw + L::OFF_WF);
   uint16_t* abar = reinterpret_cast<uint16_t*>(br_raw + L::OFF_ABAR) + cl * BR_MAXN;
@@ -280,8 +282,10 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
   const int bt = valid ? modswitch(in[n], LG) : 0;
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = lane; t < FFT_N; t += 32)
-    acc[t] = (p == 0) ? 0u : (uint32_t)((rot_coef(tv, t, r0) + 0x80000000ull) >> 32);
+  for (int t = lane; t < FFT_M; t += 32) {
+    auto top = [&](int e) { return (uint32_t)((rot_coef(tv, e, r0) + 0x80000000ull) >> 32); };
+    acc2[t] = (p == 0) ? make_uint2(0u, 0u) : make_uint2(top(t), top(t + FFT_M));
+  }
   __syncthreads();
 
   const int shift = 32 - base_log;
@@ -299,11 +303,15 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      const int s0 = j - ar, s1 = j + FFT_M - ar;
-      const uint32_t w0 = (s0 < 0) ? ~flip0 : flip0, w1 = (s1 < 0) ? ~flip0 : flip0;
-      const uint32_t g0 = acc[s0 & (FFT_N - 1)], g1 = acc[s1 & (FFT_N - 1)];
-      const uint32_t v0 = ((g0 ^ w0) - w0) - acc[j];          // (+/- g0) - acc[j]
-      const uint32_t v1 = ((g1 ^ w1) - w1) - acc[j + FFT_M];
+      // Coefficients t = j - ar and t + M of X^ar acc share the pair slot t mod M: t >= 0 reads
+      // (x, y) as they are, -M <= t < 0 reads (-y, x), t < -M reads (-x, -y).
+      const int t = j - ar;
+      const uint2 g = acc2[t & (FFT_M - 1)], own = acc2[j];
+      const bool sw = (unsigned)(t + FFT_M) < (unsigned)FFT_M;
+      const uint32_t w0 = (t < 0) ? ~flip0 : flip0, w1 = (t < -FFT_M) ? ~flip0 : flip0;
+      const uint32_t g0 = sw ? g.y : g.x, g1 = sw ? g.x : g.y;
+      const uint32_t v0 = ((g0 ^ w0) - w0) - own.x;          // (+/- g0) - acc[j]
+      const uint32_t v1 = ((g1 ^ w1) - w1) - own.y;
       // Balanced digit of the top base_log bits: arithmetic shift of the rounded 32-bit word.
       const int d0 = (int)(v0 + rnd) >> shift;
       const int d1 = (int)(v1 + rnd) >> shift;
@@ -346,8 +354,10 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      acc[j] += scaled_f64_to_top32(x[m].x);
-      acc[j + FFT_M] += scaled_f64_to_top32(x[m].y);
+      uint2 o = acc2[j];
+      o.x += scaled_f64_to_top32(x[m].x);
+      o.y += scaled_f64_to_top32(x[m].y);
+      acc2[j] = o;
     }
     __syncwarp();
   }
@@ -356,11 +366,11 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     uint64_t* o = out + (size_t)ct * (FFT_N + 1);
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32) {
-        const uint64_t v = (uint64_t)acc[t == 0 ? 0 : FFT_N - t] << 32;
+        const uint64_t v = (uint64_t)acc_at(t == 0 ? 0 : FFT_N - t) << 32;
         o[t] = (t == 0) ? v : (uint64_t)0 - v;
       }
     } else if (lane == 0) {
-      o[FFT_N] = (uint64_t)acc[0] << 32;
+      o[FFT_N] = (uint64_t)acc_at(0) << 32;
     }
   }
 }
@@ -445,14 +455,16 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   const double2* och = reinterpret_cast<const double2*>(reinterpret_cast<double*>(mlb_raw) +
                                                         (warp ^ 1) * FFT_M);
   // accumulator word t = hi[t] 2^32 + lo[t] 2^16 (the low 16 bits stay zero)
-  uint32_t* acc_hi = reinterpret_cast<uint32_t*>(mlb_raw + Y::OFF_HI) + warp * FFT_N;
-  uint16_t* acc_lo = reinterpret_cast<uint16_t*>(mlb_raw + Y::OFF_LO) + warp * FFT_N;
-  auto acc_get = [&](int t) {
-    return ((uint64_t)acc_hi[t] << 32) | ((uint64_t)acc_lo[t] << 16);
+  // with coefficients (j, j + M) side by side: hi2[j] = (hi[j], hi[j + M]), lo2 likewise
+  uint2* hi2 = reinterpret_cast<uint2*>(mlb_raw + Y::OFF_HI) + warp * FFT_M;
+  ushort2* lo2 = reinterpret_cast<ushort2*>(mlb_raw + Y::OFF_LO) + warp * FFT_M;
+  auto word = [](uint32_t hi, uint16_t lo) { return ((uint64_t)hi << 32) | ((uint64_t)lo << 16); };
+  auto acc_at = [&](int e) {
+    return e < FFT_M ? word(hi2[e].x, lo2[e].x) : word(hi2[e - FFT_M].y, lo2[e - FFT_M].y);
   };
-  auto acc_put = [&](int t, uint64_t v) {
-    acc_hi[t] = (uint32_t)(v >> 32);
-    acc_lo[t] = (uint16_t)(v >> 16);
+  auto acc_put2 = [&](int k, uint64_t v0, uint64_t v1) {
+    hi2[k] = make_uint2((uint32_t)(v0 >> 32), (uint32_t)(v1 >> 32));
+    lo2[k] = make_ushort2((uint16_t)(v0 >> 16), (uint16_t)(v1 >> 16));
   };
   const double2* ggsw_s = reinterpret_cast<const double2*>(mlb_raw + Y::OFF_GGSW);
   const uint32_t bar = tc::smem_u32(mlb_raw + Y::OFF_BAR);
@@ -475,7 +487,8 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   const uint64_t* tv = tv_of(sel, valid ? ct : 0);
   const int bt = valid ? modswitch(in[n], LG) : 0;
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = lane; t < FFT_N; t += 32) acc_put(t, (p == 0) ? 0 : rot_coef(tv, t, r0));
+  for (int t = lane; t < FFT_M; t += 32)
+    acc_put2(t, (p == 0) ? 0 : rot_coef(tv, t, r0), (p == 0) ? 0 : rot_coef(tv, t + FFT_M, r0));
   uint64_t a_next = valid ? in[0] : 0;  // mask coefficient of the next CMux, loaded one ahead
   __syncthreads();
 
@@ -515,12 +528,18 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int j = lane + 32 * (4 * g + q);
-          const int s0 = j - ar, s1 = j + FFT_M - ar;
-          const uint64_t n0 = (uint64_t)(int64_t)(s0 >> 31) ^ flip;
-          const uint64_t n1 = (uint64_t)(int64_t)(s1 >> 31) ^ flip;
-          const uint64_t g0 = acc_get(s0 & (FFT_N - 1)), g1 = acc_get(s1 & (FFT_N - 1));
-          const uint64_t v0 = ((g0 ^ n0) - n0) - acc_get(j) + vk_off;
-          const uint64_t v1 = ((g1 ^ n1) - n1) - acc_get(j + FFT_M) + vk_off;
+          // coefficients t = j - ar and t + M of X^ar acc share the pair slot t mod M: t >= 0
+          // reads (x, y) as they are, -M <= t < 0 reads (-y, x), t < -M reads (-x, -y)
+          const int tr = j - ar;
+          const uint2 gh = hi2[tr & (FFT_M - 1)], oh = hi2[j];
+          const ushort2 gl = lo2[tr & (FFT_M - 1)], ol = lo2[j];
+          const bool sw = (unsigned)(tr + FFT_M) < (unsigned)FFT_M;
+          const uint64_t n0 = (tr < 0 ? ~0ull : 0ull) ^ flip;
+          const uint64_t n1 = (tr < -FFT_M ? ~0ull : 0ull) ^ flip;
+          const uint64_t ga = word(gh.x, gl.x), gb = word(gh.y, gl.y);
+          const uint64_t g0 = sw ? gb : ga, g1 = sw ? ga : gb;
+          const uint64_t v0 = ((g0 ^ n0) - n0) - word(oh.x, ol.x) + vk_off;
+          const uint64_t v1 = ((g1 ^ n1) - n1) - word(oh.y, ol.y) + vk_off;
           t[4 * q + 0] = (uint32_t)v0;
           t[4 * q + 1] = (uint32_t)(v0 >> 32);
           t[4 * q + 2] = (uint32_t)v1;
@@ -615,8 +634,10 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      acc_put(j, acc_get(j) + scaled_f64_to_top48(x[m].x));
-      acc_put(j + FFT_M, acc_get(j + FFT_M) + scaled_f64_to_top48(x[m].y));
+      const uint2 h = hi2[j];
+      const ushort2 l = lo2[j];
+      acc_put2(j, word(h.x, l.x) + scaled_f64_to_top48(x[m].x),
+               word(h.y, l.y) + scaled_f64_to_top48(x[m].y));
     }
     __syncwarp();
   }
@@ -636,9 +657,9 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
     uint64_t* o = out + (size_t)ct * (FFT_N + 1);
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32)
-        o[t] = (t == 0) ? acc_get(0) : (uint64_t)0 - acc_get(FFT_N - t);
+        o[t] = (t == 0) ? acc_at(0) : (uint64_t)0 - acc_at(FFT_N - t);
     } else if (lane == 0) {
-      o[FFT_N] = acc_get(0);
+      o[FFT_N] = acc_at(0);
     }
   }
 }
