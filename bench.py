@@ -287,6 +287,9 @@ def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6)), B=409
         pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
         pnb.blind_rotate(keys, tv, small, out=o)
         ok = bool(np.array_equal(pnb.decrypt_vec(keys, o).cpu().numpy(), lut[msgs]))
+        ph = pnb.phase(keys, o).cpu().numpy().view(np.uint64)
+        err = (ph - lut[msgs].astype(np.uint64) * np.uint64(keys.params.delta())).view(np.int64)
+        log2_std = float(np.log2(err.astype(np.float64).std()))
         reps, ms = 3, 0.0
         for _ in range(reps):
             flush.zero_()
@@ -299,7 +302,8 @@ def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6)), B=409
             ms += a.elapsed_time(b)
         ms /= reps
         out.append({"base_log": base_log, "levels": levels, "batch": B,
-                    "pbs_per_second": B / (ms * 1e-3), "decrypt_ok": ok})
+                    "pbs_per_second": B / (ms * 1e-3), "decrypt_ok": ok,
+                    "log2_noise_std": log2_std})
         del ct, small, ks_ws, o
         keys.free()
     return out
