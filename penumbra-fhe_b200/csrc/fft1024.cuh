@@ -160,29 +160,31 @@ __device__ __forceinline__ void untwist(double2 (&x)[FFT_R]) {
 }
 
 // Swizzled 32x32 transpose through a per-warp shared buffer of 1024 double2.
-// Writes element (row = register index, col = lane) and reads back (row = lane, col = register).
+// Writes element (row = register index, col = lane) to slot row * 32 + (col ^ row) and reads
+// back (row = lane, col = register): both patterns touch 32 distinct columns of distinct rows,
+// so neither has bank conflicts, and each address is one XOR on a per-lane base.
 __device__ __forceinline__ void warp_transpose(double2 (&x)[FFT_R], double2* buf, int lane) {
 #pragma unroll
-  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r];
+  for (int r = 0; r < 32; ++r) buf[r * 32 + (lane ^ r)] = x[r];
   __syncwarp();
 #pragma unroll
-  for (int q = 0; q < 32; ++q) x[q] = buf[lane * 32 + ((q + lane) & 31)];
+  for (int q = 0; q < 32; ++q) x[q] = buf[lane * 32 + (q ^ lane)];
   __syncwarp();
 }
 
 // The same transpose through an 8 KB buffer of 1024 doubles: real parts, then imaginary parts.
 __device__ __forceinline__ void warp_transpose_half(double2 (&x)[FFT_R], double* buf, int lane) {
 #pragma unroll
-  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r].x;
+  for (int r = 0; r < 32; ++r) buf[r * 32 + (lane ^ r)] = x[r].x;
   __syncwarp();
 #pragma unroll
-  for (int q = 0; q < 32; ++q) x[q].x = buf[lane * 32 + ((q + lane) & 31)];
+  for (int q = 0; q < 32; ++q) x[q].x = buf[lane * 32 + (q ^ lane)];
   __syncwarp();
 #pragma unroll
-  for (int r = 0; r < 32; ++r) buf[r * 32 + ((lane + r) & 31)] = x[r].y;
+  for (int r = 0; r < 32; ++r) buf[r * 32 + (lane ^ r)] = x[r].y;
   __syncwarp();
 #pragma unroll
-  for (int q = 0; q < 32; ++q) x[q].y = buf[lane * 32 + ((q + lane) & 31)];
+  for (int q = 0; q < 32; ++q) x[q].y = buf[lane * 32 + (q ^ lane)];
   __syncwarp();
 }
 
@@ -240,10 +242,10 @@ __device__ __forceinline__ void fft_inverse_h(double2 (&x)[FFT_R], double* buf, 
 }
 
 // Twiddle table T held once in shared memory for both directions.  Element (a, b) of the 32x32
-// table lives at a*32 + ((a+b) & 31): the forward transform reads row r across the lanes and
-// the inverse reads the transpose (its twiddle at lane l, register n is conj(T(l, n))); with
-// this swizzle both patterns are bank-conflict free.
-__device__ __forceinline__ int tw_swz(int a, int b) { return a * 32 + ((a + b) & 31); }
+// table lives at a*32 + (a ^ b): the forward transform reads row r across the lanes and the
+// inverse reads the transpose (its twiddle at lane l, register n is conj(T(l, n))); with this
+// swizzle both patterns are bank-conflict free.
+__device__ __forceinline__ int tw_swz(int a, int b) { return a * 32 + (a ^ b); }
 
 template <bool CB = true>
 __device__ __forceinline__ void fft_forward_s(double2 (&x)[FFT_R], double* buf, int lane,
