@@ -616,6 +616,35 @@ def run_gpu(args):
     return 0
 
 
+LAUNCH_TIME_SCALE = {"ns": 1e-6, "nsecond": 1e-6, "us": 1e-3, "usecond": 1e-3, "ms": 1.0,
+                     "msecond": 1.0, "s": 1e3, "second": 1e3}
+
+
+def summarize_launches(path):
+    """Per-kernel launches, total device time and share of an ncu launch list
+    (`ncu --metrics gpu__time_duration.sum --csv --log-file <path>`; cold-cache, serialised)."""
+    import collections
+    import csv
+    with open(path) as f:
+        rows = list(csv.reader(f))
+    hi = next(i for i, r in enumerate(rows) if "Kernel Name" in r)
+    hdr, data = rows[hi], rows[hi + 1:]
+    ki, mi = hdr.index("Kernel Name"), hdr.index("Metric Name")
+    vi, ui = hdr.index("Metric Value"), hdr.index("Metric Unit")
+    agg = collections.defaultdict(lambda: [0, 0.0])
+    for r in data:
+        if len(r) <= vi or r[mi] != "gpu__time_duration.sum":
+            continue
+        name = r[ki].split("(")[0].strip()
+        agg[name][0] += 1
+        agg[name][1] += float(r[vi].replace(",", "")) * LAUNCH_TIME_SCALE[r[ui]]
+    tot = sum(v[1] for v in agg.values())
+    print(f"{'kernel':62s} {'launches':>8s} {'total ms':>10s} {'share':>7s}")
+    for k, (n, t) in sorted(agg.items(), key=lambda x: -x[1][1]):
+        print(f"{k[:62]:62s} {n:8d} {t:10.2f} {100 * t / tot:6.2f}%")
+    print(f"{'all':62s} {sum(v[0] for v in agg.values()):8d} {tot:10.2f}")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -630,6 +659,8 @@ def main():
                     help="samples of the Linear 784->128 contraction leg (0 skips it)")
     ap.add_argument("--sweep", type=int, default=1,
                     help="PBS/s across batch sizes 1..65536 (rank 0)")
+    ap.add_argument("--summarize-launches", metavar="CSV", default=None,
+                    help="print the per-kernel table of an ncu launch list and exit")
     ap.add_argument("--key-sets", type=int, default=1,
                     help="PBS/s of the multi-level key sets at batch 4096 (rank 0)")
     ap.add_argument("--noise", type=int, default=1,
@@ -637,6 +668,9 @@ def main():
     ap.add_argument("--mlp-batch", type=int, default=32,
                     help="encrypted MLP samples per GPU (0 skips the MLP leg)")
     args = ap.parse_args()
+    if args.summarize_launches:
+        summarize_launches(args.summarize_launches)
+        return 0
     if args.impl == "reference":
         return run_reference(args)
     return run_gpu(args)
