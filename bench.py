@@ -153,7 +153,7 @@ def run_reference(args):
     world, rank, _ = dist_setup(args)
     if rank != 0:
         return 0
-    steps, warm = args.steps, max(1, min(args.warmup, 1))
+    steps, warm = args.steps, max(args.warmup, 0)
     per_step = args.ref_samples
     v, info = cpu_reference_run(args, per_step, warm, steps)
     line = {
