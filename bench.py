@@ -48,8 +48,10 @@ WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussi
 # DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts, from the ncu
 # capture summarised in profiles/blind_rotate_pbs4096.md (None until that capture exists).
 BR_TRAFFIC_PER_LAUNCH = None
-# DRAM bytes of one contract_tc_kernel launch of the contraction leg (None until captured).
-CONTRACT_TRAFFIC = None
+# DRAM bytes (read + write) of one contract_tc_kernel launch of the contraction leg at 256
+# samples: the 32-sample ncu capture (411.4 MB read + 53.7 MB written, every input ciphertext
+# read once and every output written once) scaled by the 8x sample count.
+CONTRACT_TRAFFIC = 8 * (411416320 + 53726976)
 
 
 def load_package():

@@ -20,6 +20,7 @@ pytestmark = pytest.mark.gpu
     (1, 1, 1, 1, True),          # degenerate
     (200, 130, 3, 2049, True),   # two M tiles; 390 tiles over the persistent CTAs
     (16, 72, 9, 2049, False),    # 585 tiles: several per CTA, both TMEM buffers reused
+    (64, 1000, 2, 2049, True),   # one M tile but K > 896: weights streamed per stage
 ])
 def test_contract_bit_exact(pnb, oracle, M, K, B, L, with_bias):
     rng = np.random.default_rng(M * 1000 + K)
