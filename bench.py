@@ -45,9 +45,10 @@ SEED = 20241201
 FLOP_PER_PBS = 834 * (4 * 51200 + 32768)  # 1.981e8 FFT-equivalent FP64 flop (n=834, N=2048)
 WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussian noise, "
             "uniform 4-bit messages, random 16-entry LUT")
-# DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts, from the ncu
-# capture summarised in profiles/blind_rotate_pbs4096.md (None until that capture exists).
-BR_TRAFFIC_PER_LAUNCH = None
+# DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts: a one-pass ncu
+# capture of the timed launch of this workload (191.4 MB read: the 54.7 MB Fourier key about
+# three times over the launch's seven block waves plus the small ciphertexts; 58.3 MB written).
+BR_TRAFFIC_PER_LAUNCH = 191380000 + 58270000
 # DRAM bytes (read + write) of one contract_tc_kernel launch of the contraction leg at 256
 # samples: the 32-sample ncu capture (411.4 MB read + 53.7 MB written, every input ciphertext
 # read once and every output written once) scaled by the 8x sample count.
