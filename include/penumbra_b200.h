@@ -166,6 +166,12 @@ int pnb_device_status(int device, int* status_out);
  * roofline denominator of the blind rotation.  No reference counterpart. */
 int pnb_measure_fp64_peak(int device, double* tflops_out);
 
+/* Run the kernels' bounded mbarrier wait against a barrier that is never completed, with a limit
+ * of `polls` polls (1..2^24): *warps_gave_up_out receives the number of waiting warps (2) that
+ * gave up and reported it instead of hanging; the context stays usable.  The timeout path of the
+ * device-side failure detection, exercised without a fault.  No reference counterpart. */
+int pnb_wait_probe(int device, unsigned polls, int* warps_gave_up_out);
+
 /* ---- Graph evaluation ------------------------------------------------------------------
  * The IR graph (a model.fhe document), compiled into a batched ciphertext program and run on
  * one GPU.  Every tensor element is one big-key LWE ciphertext holding the exact integer at a

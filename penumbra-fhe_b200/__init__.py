@@ -88,6 +88,7 @@ _SIGS = {
                                          C.c_int, C.c_void_p]),
     "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
     "pnb_device_status": (C.c_int, [C.c_int, C.POINTER(C.c_int)]),
+    "pnb_wait_probe": (C.c_int, [C.c_int, C.c_uint, C.POINTER(C.c_int)]),
     "pnb_graph_load": (C.c_int, [C.c_char_p, C.c_size_t, C.POINTER(C.c_void_p)]),
     "pnb_graph_free": (C.c_int, [C.c_void_p]),
     "pnb_graph_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
@@ -418,6 +419,13 @@ def device_status(device: int = 0) -> int:
     """Read and clear the tensor-core kernels' status word (0 = every bounded wait completed)."""
     v = C.c_int()
     _check("pnb_device_status", lib().pnb_device_status(device, C.byref(v)))
+    return v.value
+
+
+def wait_probe(device: int = 0, polls: int = 1000) -> int:
+    """Warps of a probe kernel that gave up a bounded wait on a never-completed barrier."""
+    v = C.c_int()
+    _check("pnb_wait_probe", lib().pnb_wait_probe(device, polls, C.byref(v)))
     return v.value
 
 

@@ -354,4 +354,15 @@ int pnb_measure_fp64_peak(int device, double* tflops_out) {
   return measure_fp64_peak(tflops_out);
 }
 
+int pnb_wait_probe(int device, unsigned polls, int* warps_gave_up_out) {
+  if (!warps_gave_up_out) { set_error("warps_gave_up_out is NULL"); return PNB_ERR_INVALID; }
+  if (polls < 1 || polls > (1u << 24)) {
+    set_error("wait probe: polls must be in 1..2^24 (got %u)", polls);
+    return PNB_ERR_INVALID;
+  }
+  DeviceGuard g(device);
+  if (g.rc) return g.rc;
+  return wait_probe(polls, warps_gave_up_out);
+}
+
 }  // extern "C"

@@ -246,7 +246,6 @@ int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
   lin_kernel<<<(unsigned)((rows + 1) / 2), 256, 0, st>>>(a);
   PNB_CHECK_LAUNCH("lin_kernel(bootstrap input)");
   const pnb_keys* K = ev->keys[I.level];
-  const int64_t n1 = ev->client->p.n + 1;
   for (int64_t r0 = 0; r0 < rows; r0 += ev->max_pbs_rows) {
     const int cnt = (int)std::min<int64_t>(ev->max_pbs_rows, rows - r0);
     uint64_t* x = ev->bufs[I.dst] + (size_t)r0 * L;

@@ -4,6 +4,7 @@
 
 #include "pnb_internal.cuh"
 #include "pnb_keys.h"
+#include "tc_primitives.cuh"
 
 namespace pnb {
 
@@ -68,6 +69,33 @@ int measure_fp64_peak(double* tflops) {
   PNB_CUDA(cudaFree(d));
   const double flops = 2.0 * 8 * (double)iters * blocks * threads;
   *tflops = flops / (best * 1e-3) / 1e12;
+  return PNB_OK;
+}
+
+// The bounded mbarrier wait of the rotation, keyswitch and contraction kernels, run against a
+// barrier that nothing completes: every thread gives up after `polls` polls and the block
+// records that it did.  Nothing is in flight on the barrier, so the block exits cleanly and the
+// context stays usable -- the property the real kernels rely on when a copy never lands.
+__global__ void wait_probe_kernel(uint32_t polls, int* gave_up) {
+  __shared__ __align__(8) uint64_t bar_word;
+  const uint32_t bar = tc::smem_u32(&bar_word);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar, 1);  // one arrival expected, none ever made
+    tc::fence_mbar_init();
+  }
+  __syncthreads();
+  const bool done = tc::mbar_wait(bar, 0u, polls);
+  if (!__all_sync(0xffffffffu, done) && (threadIdx.x & 31) == 0) atomicAdd(gave_up, 1);
+}
+
+int wait_probe(uint32_t polls, int* warps_gave_up) {
+  int* d = nullptr;
+  PNB_CUDA(cudaMalloc(&d, sizeof(int)));
+  PNB_CUDA(cudaMemset(d, 0, sizeof(int)));
+  wait_probe_kernel<<<1, 64>>>(polls, d);
+  PNB_CHECK_LAUNCH("wait_probe_kernel");
+  PNB_CUDA(cudaMemcpy(warps_gave_up, d, sizeof(int), cudaMemcpyDeviceToHost));
+  PNB_CUDA(cudaFree(d));
   return PNB_OK;
 }
 

@@ -40,6 +40,10 @@ static std::mutex g_tab_mu;
 static FftTables g_tab[64];
 static bool g_tab_ok[64];
 
+// T(r, l) = rho_r^l, rho_r = exp(i pi (1 + 4 bitrev(r)) / 2048): angle pi e / 2048 with the
+// exponent e reduced mod 4096 in integers first, evaluated in long double on the host.
+static double2 mid_twiddle(int r, int l);
+
 static int bitrev5(int v) {
   int r = 0;
   for (int b = 0; b < 5; ++b)
@@ -57,19 +61,11 @@ int fft_tables_get(FftTables* out) {
   std::lock_guard<std::mutex> lk(g_tab_mu);
   if (!g_tab_ok[dev]) {
     const int M = FFT_M;
-    const long double PI = 3.141592653589793238462643383279502884L;
     std::vector<double2> wf(M), wi(M);
-    // T(r, l) = rho_r^l, rho_r = exp(i pi (1 + 4 bitrev(r)) / 2048): angle pi e / 2048 with the
-    // exponent reduced mod 4096 in integers first.
-    auto T = [&](int r, int l) {
-      const long long e = ((long long)l * (1 + 4 * bitrev5(r))) % 4096;
-      const long double ang = PI * (long double)e / 2048.0L;
-      return make_double2((double)cosl(ang), (double)sinl(ang));
-    };
     for (int r = 0; r < 32; ++r)
       for (int l = 0; l < 32; ++l) {
-        wf[r * 32 + l] = T(r, l);
-        const double2 t = T(l, r);
+        wf[r * 32 + l] = mid_twiddle(r, l);
+        const double2 t = mid_twiddle(l, r);
         wi[r * 32 + l] = make_double2(t.x, -t.y);
       }
     FftTables t{};
@@ -82,6 +78,13 @@ int fft_tables_get(FftTables* out) {
   }
   *out = g_tab[dev];
   return PNB_OK;
+}
+
+static double2 mid_twiddle(int r, int l) {
+  const long double PI = 3.141592653589793238462643383279502884L;
+  const long long e = ((long long)l * (1 + 4 * bitrev5(r))) % 4096;
+  const long double ang = PI * (long double)e / 2048.0L;
+  return make_double2((double)cosl(ang), (double)sinl(ang));
 }
 
 // True when the current device's FFT tables exist (never allocates).

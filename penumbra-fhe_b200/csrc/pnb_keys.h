@@ -43,6 +43,7 @@ int encrypt_lwe(const pnb_keys* K, const int64_t* msg, uint64_t delta, uint64_t 
 int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count, int small,
               cudaStream_t st);
 int measure_fp64_peak(double* tflops);
+int wait_probe(uint32_t polls, int* warps_gave_up);
 int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                     const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st);
 // As lwe_contract_gather, with group g = b*P + p written to output row (b*M + m)*P + p

@@ -191,3 +191,15 @@ def test_multilevel_bootstrap(pnb, oracle, beta, level):
     assert 0.5 < ratio < 2.0, f"noise variance ratio {ratio:.3f}"
     # the whole point of the extra levels: far below the one-level set's ~2^49
     assert np.log2(gpu_noise.std()) < {2: 43.5, 3: 40.0, 4: 38.0, 6: 35.0}[level]
+
+
+def test_bounded_wait_gives_up_and_context_survives(pnb, gkeys):
+    """A kernel waiting on an mbarrier that nothing completes (the kernels' bounded wait) gives
+    up after its poll limit and reports it; the same context then still bootstraps exactly."""
+    assert pnb.wait_probe(0, polls=2000) == 2
+    lut = [(3 * v + 1) % 16 for v in range(16)]
+    tv = pnb.test_vector(gkeys, lut)
+    msgs = np.arange(64) % 16
+    out = pnb.pbs_batch(gkeys, tv, pnb.encrypt(gkeys, torch.tensor(msgs), seed=3))
+    assert np.array_equal(pnb.decrypt_vec(gkeys, out).cpu().numpy(), np.array(lut)[msgs])
+    assert pnb.device_status(0) == 0
