@@ -192,6 +192,13 @@ __global__ void __launch_bounds__(CT_THREADS, 1) contract_tc_kernel(
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     for (; released < kb_global; ++released) tc::mbar_arrive(full(released % STAGES));
+    if (warp == 0 && lane == 0) {
+      // No W tile may still be landing when the block exits.  Every producer has arrived for
+      // every stage it filled (above), so the last use of each stage completes exactly when its
+      // W tile has landed: observe that (bounded) -- immediate unless a wait ran out.
+      for (int k = kb_global > STAGES ? kb_global - STAGES : 0; k < kb_global; ++k)
+        (void)tc::mbar_wait(full(k % STAGES), (uint32_t)(k / STAGES) & 1u, CT_WAIT_LIMIT);
+    }
   } else if (warp == CT_MMA_WARP) {
     // ---------------- MMA issue (one elected lane) --------------------------------------------
     if (lane == 0) {

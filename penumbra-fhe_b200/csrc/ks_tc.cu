@@ -152,6 +152,7 @@ __global__ void __launch_bounds__(192, 1) ks_gemm_kernel(const __grid_constant__
 
   if (warp == 0) {
     if (lane == 0) {  // TMA producer
+      int issued = 0;
       for (int kb = 0; kb < k_blocks; ++kb) {
         const int s = kb % KS_STAGES;
         const uint32_t ph = (uint32_t)(kb / KS_STAGES) & 1u;
@@ -164,7 +165,12 @@ __global__ void __launch_bounds__(192, 1) ks_gemm_kernel(const __grid_constant__
         tc::tma_load_2d(a_s, &tmA, kb * KS_BK, m0, full(s));
         tc::tma_load_2d(b_s, &tmB, nb0, kb * KS_BK, full(s));
         tc::tma_load_2d(b_s + KS_BK * 128, &tmB, nb0 + 128, kb * KS_BK, full(s));
+        issued = kb + 1;
       }
+      // No copy may still be landing when the block exits: observe (bounded) the completion
+      // of the last use of every stage -- immediate unless a wait above ran out.
+      for (int kb = issued > KS_STAGES ? issued - KS_STAGES : 0; kb < issued; ++kb)
+        (void)tc::mbar_wait(full(kb % KS_STAGES), (uint32_t)(kb / KS_STAGES) & 1u, KS_WAIT_LIMIT);
     }
   } else if (warp == 1) {
     if (lane == 0) {  // MMA issuer

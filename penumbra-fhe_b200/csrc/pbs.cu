@@ -347,7 +347,11 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     }
     // Every warp is done with GGSW i: stage GGSW i+1 while the inverse FFTs run.
     __syncthreads();
-    if (*abort_s) break;  // uniform: read by every thread after the same barrier
+    if (*abort_s) {  // uniform: read by every thread after the same barrier
+      // the copy of GGSW i may still be landing: let it (bounded) before the block exits
+      if (threadIdx.x == 0) (void)tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT);
+      break;
+    }
     if (threadIdx.x == 0 && i + 1 < n) {
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
