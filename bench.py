@@ -360,8 +360,9 @@ def noise_leg(pnb, keys, dev, total=100352):
             "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2))}
 
 
-def mlp_cpu_baseline(plan, graph, per_level: int = 32):
-    """CPU restatement of the same encrypted MLP program, timed on a bounded sample.
+def program_cpu_baseline(plan, graph, per_level: int = 32):
+    """CPU restatement of the same encrypted program (a graph whose first node is a Linear
+    layer), timed on a bounded sample.
 
     Every key set the program uses gets `per_level` oracle f64-FFT bootstraps (keyswitch +
     blind rotation + extraction, all host threads); the first layer's contraction is timed on
@@ -395,23 +396,24 @@ def mlp_cpu_baseline(plan, graph, per_level: int = 32):
     sec += tc
     return {"value": 1.0 / sec, "unit": "samples/s", "cores": threads, "kind": "port",
             "sample": f"{per_level} oracle bootstraps per key set, extrapolated by the "
-                      f"program's counts [{'; '.join(timed)}] + the 784->128 contraction of one "
-                      f"sample ({1e3 * tc:.1f} ms)"}
+                      f"program's counts [{'; '.join(timed)}] + the {W.shape[1]}->{W.shape[0]} "
+                      f"contraction of one sample ({1e3 * tc:.1f} ms)"}
 
 
-def mlp_leg(args, pnb, world, rank, local, dist, dev):
-    """Encrypted MLP inference over a sample shard per rank; returns the "mlp" object."""
+def graph_leg(args, pnb, world, rank, local, dist, dev, graph, B, seed, workload, metric,
+              cpu_baseline=None):
+    """Encrypted inference of `graph` over a B-sample shard per rank: device time of the
+    evaluation plus the output all-gather, and end to end with the host copies; rank 0 decrypts
+    the first samples of every rank and compares them with the cleartext graph."""
     import numpy as np
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ir_eval
-    with open(os.path.join(ROOT, "tests", "golden", "cfg4_mlp.json")) as f:
-        graph = json.load(f)["graph"]
     plan = pnb.Plan(pnb.Graph(graph))
     ev = pnb.Evaluator(plan, device=local, seed=SEED)  # identical keys on every rank
-    B = args.mlp_batch
-    rng = np.random.default_rng(SEED + 100 + rank)
-    x = rng.integers(0, 64, (B, plan.input_elems))
+    hi = (1 << graph["input_bits"]) - 1
+    rng = np.random.default_rng(seed + rank)
+    x = rng.integers(0, hi + 1, (B, plan.input_elems))
     ct = ev.encrypt(x, seed=SEED + 7, first_index=rank * B * plan.input_elems)
     ev.reserve(B)
     ev.evaluate(ct[:1])  # warm-up
@@ -447,34 +449,67 @@ def mlp_leg(args, pnb, world, rank, local, dist, dev):
         t_dev, t_e2e = float(t[0]), float(t[1])
     ok = None
     if rank == 0:
-        # decrypt the gathered outputs of every rank's first samples and compare to the
-        # cleartext graph on the same integers
         got = ev.decrypt(h_out.to(dev)).cpu().numpy()
         ok = True
         for r in range(world):
-            xr = np.random.default_rng(SEED + 100 + r).integers(0, 64, (B, plan.input_elems))
+            xr = np.random.default_rng(seed + r).integers(0, hi + 1, (B, plan.input_elems))
             for i in range(min(B, 2)):
-                want = ir_eval.evaluate(graph, {"x": xr[i].tolist()})[graph["outputs"][0]]
-                ok = ok and got[r * B + i].tolist() == want
+                want = ir_eval.evaluate(graph, {graph["inputs"][0]: xr[i].tolist()})
+                ok = ok and got[r * B + i].tolist() == want[graph["outputs"][0]]
     return {
-        "metric": "encrypted_mlp_samples_per_second", "value": world * B / (t_dev * 1e-3),
+        "metric": metric, "value": world * B / (t_dev * 1e-3),
         "unit": "samples/s", "samples_per_gpu": B, "global_batch": world * B,
         "scaling": "weak", "ms": t_dev,
-        "config": {"workload": "MLP 784-128-128-10, ReLU fused in Requant, PTQ n_bits=6 "
-                               "(reference quantizer graph), 6-bit inputs",
+        "config": {"workload": workload,
                    "parallelism": f"samples sharded over {world} GPU(s), outputs all-gathered "
                                   "over NCCL"},
         "bootstraps_per_sample": plan.pbs_per_sample,
         "bootstraps_by_key_set": [{"base_log": b, "levels": l, "per_sample": c}
                                   for b, l, c in plan.key_sets()],
-        "cpu_baseline": (mlp_cpu_baseline(plan, graph)
-                         if rank == 0 and world == 1 and not args.no_cpu_baseline else None),
+        "cpu_baseline": (cpu_baseline(plan, graph) if cpu_baseline is not None and rank == 0
+                         and world == 1 and not args.no_cpu_baseline else None),
         "allgather_ms": t_gather,
         "e2e": {"value": world * B / (t_e2e * 1e-3), "unit": "samples/s",
                 "h2d_bytes_per_step": int(h_in.numel() * 8),
                 "d2h_bytes_per_step": int(h_out.numel() * 8) if rank == 0 else 0},
         "decrypt_ok": ok,
     }
+
+
+def mlp_leg(args, pnb, world, rank, local, dist, dev):
+    """Encrypted MLP 784-128-128-10 (the reference quantizer's graph for that configuration)."""
+    with open(os.path.join(ROOT, "tests", "golden", "cfg4_mlp.json")) as f:
+        graph = json.load(f)["graph"]
+    return graph_leg(args, pnb, world, rank, local, dist, dev, graph, args.mlp_batch,
+                     SEED + 100,
+                     "MLP 784-128-128-10, ReLU fused in Requant, PTQ n_bits=6 (reference "
+                     "quantizer graph), 6-bit inputs",
+                     "encrypted_mlp_samples_per_second", cpu_baseline=program_cpu_baseline)
+
+
+def linear_requant_graph():
+    """Encrypted Linear 784 -> 128 with int4 weights U[-8, 7] from a seed and 6-bit inputs,
+    followed by a ReLU-fused requantization to 2 bits (shift 11, round bias 1024)."""
+    import numpy as np
+    rng = np.random.default_rng(3)
+    W = rng.integers(-8, 8, (128, 784)).tolist()
+    nodes = [{"name": "fc", "inputs": ["x"], "outputs": ["acc"],
+              "op": {"op_type": "Linear", "weights": W, "bias": [0] * 128, "weight_bits": 4}},
+             {"name": "rq", "inputs": ["acc"], "outputs": ["y"],
+              "op": {"op_type": "Requant", "shift": 11, "mult": 1, "round_bias": 1024,
+                     "out_bits": 2, "clamp_lut": [0, 1, 2, 3]}}]
+    return {"schema_version": "0.6.0", "num_blocks": 12, "input_bits": 6, "inputs": ["x"],
+            "outputs": ["y"], "nodes": nodes}
+
+
+def linear_requant_leg(args, pnb, world, rank, local, dist, dev):
+    """The Linear 784 -> 128 + Requant configuration end to end (contraction + bootstraps)."""
+    return graph_leg(args, pnb, world, rank, local, dist, dev, linear_requant_graph(),
+                     args.lr_batch, SEED + 200,
+                     "Linear 784->128 (int4 weights U[-8,7]) + ReLU-Requant to 2 bits, 6-bit "
+                     "inputs, N=2048 parameter set",
+                     "encrypted_linear_requant_samples_per_second",
+                     cpu_baseline=program_cpu_baseline)
 
 
 def run_gpu(args):
@@ -575,6 +610,8 @@ def run_gpu(args):
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
     mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
+    lin_rq = (None if args.lr_batch <= 0
+              else linear_requant_leg(args, pnb, world, rank, local, dist, dev))
     contraction = None if args.contract_batch <= 0 else contraction_leg(args, pnb, local, dev,
                                                                            flush)
     noise = noise_leg(pnb, keys, dev) if (rank == 0 and args.noise) else None
@@ -608,6 +645,7 @@ def run_gpu(args):
             "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
             "decrypt_ok": decrypt_ok and e2e_ok,
             "mlp": mlp,
+            "linear_requant": lin_rq,
             "contraction": contraction,
             "noise": noise,
             "pbs_batch_sweep": sweep,
@@ -668,6 +706,8 @@ def main():
                     help="PBS/s of the multi-level key sets at batch 4096 (rank 0)")
     ap.add_argument("--noise", type=int, default=1,
                     help="measure the bootstrap output noise over ~1e5 bootstraps (rank 0)")
+    ap.add_argument("--lr-batch", type=int, default=64,
+                    help="samples per GPU of the Linear 784->128 + Requant leg (0 skips it)")
     ap.add_argument("--mlp-batch", type=int, default=32,
                     help="encrypted MLP samples per GPU (0 skips the MLP leg)")
     args = ap.parse_args()
