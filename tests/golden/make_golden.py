@@ -10,7 +10,9 @@ inputs with the reference input spec, runs the reference integer oracle
 (``python/penumbra/reference.py`` ``evaluate_graph_int``) and writes the IR graph, the
 quantized inputs and every intermediate tensor to ``tests/golden/<name>.json``.  It also
 re-evaluates the reference's committed fixtures (``examples/mnist/phase2_fixture.json``,
-``phase4_cnn_fixture.json``) and checks the oracle against their ``expected_*`` values.
+``phase4_cnn_fixture.json``, and the heavy models its golden tests skip: ``phase5_digits``,
+``phase5_qat``, ``phase6_onnx``, ``phase6_sklearn``, ``examples/faces/phase7_faces``) and checks
+the oracle against their ``expected_*`` values.
 
 Only this script reads the reference; tests and the GPU box read the JSON it writes.
 
@@ -140,7 +142,13 @@ def main():
 
     # The reference's committed fixtures: re-evaluate and check their expected values.
     for fx, key in (("examples/mnist/phase4_cnn_fixture.json", "expected_logits"),
-                    ("examples/mnist/phase2_fixture.json", "expected_labels")):
+                    ("examples/mnist/phase2_fixture.json", "expected_labels"),
+                    # the models the reference's own golden tests skip as minutes per sample
+                    ("examples/mnist/phase5_digits_fixture.json", "expected_logits"),
+                    ("examples/mnist/phase5_qat_fixture.json", "expected_logits"),
+                    ("examples/mnist/phase6_onnx_fixture.json", "expected_logits"),
+                    ("examples/mnist/phase6_sklearn_fixture.json", "expected_logits"),
+                    ("examples/faces/phase7_faces_fixture.json", "expected_logits")):
         d = json.load(open(os.path.join(REF, fx)))
         g = P.ir.Graph.from_json(json.dumps(d["graph"]))
         outs = [P.evaluate_graph_int(g, {"x": x})[g.outputs[0]] for x in d["test_inputs"]]
