@@ -202,6 +202,14 @@ int pnb_graph_info(const pnb_graph* graph, int* num_nodes, int* num_blocks, int*
  * exceeded).  Replaces: check_graph_bit_width_budget (runtime/src/eval.rs:237-276). */
 int pnb_graph_check_budget(const pnb_graph* graph);
 
+/* Output and internal bit widths of one op (its IR payload, a JSON object such as a node's
+ * "op") consuming tensors of the given widths, after the op's validation (PNB_ERR_INVALID +
+ * the reference's message when it fails).  Replaces: Op::output_bits_n / Op::internal_bits_n
+ * (runtime/src/ops/mod.rs:116-138) with the per-op rules of ops/{linear,conv2d,pool,requant,
+ * activation,argmax,add}.rs. */
+int pnb_op_bits(const char* op_json, size_t len, const int* input_bits, int n_inputs,
+                int* output_bits, int* internal_bits);
+
 /* Compile a graph for a parameter set.  input_lens (may be NULL; one entry per graph input, 0 =
  * infer from the consumer) gives the element count of each graph input; input_lo/input_hi bound
  * every graph-input value; margin_sigmas (<= 0: 7) is the decision margin of every bootstrap in

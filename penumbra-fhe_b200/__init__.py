@@ -21,7 +21,7 @@ __all__ = [
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
-    "gather_shards", "evaluate_sharded",
+    "gather_shards", "evaluate_sharded", "op_bits", "wait_probe",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -94,6 +94,8 @@ _SIGS = {
     "pnb_graph_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
                                  C.POINTER(C.c_int)]),
     "pnb_graph_check_budget": (C.c_int, [C.c_void_p]),
+    "pnb_op_bits": (C.c_int, [C.c_char_p, C.c_size_t, C.POINTER(C.c_int), C.c_int,
+                             C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "pnb_plan_create": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                   C.c_double, C.POINTER(C.c_void_p)]),
     "pnb_plan_free": (C.c_int, [C.c_void_p]),
@@ -420,6 +422,17 @@ def device_status(device: int = 0) -> int:
     v = C.c_int()
     _check("pnb_device_status", lib().pnb_device_status(device, C.byref(v)))
     return v.value
+
+
+def op_bits(op: dict, input_bits: list[int]) -> tuple[int, int]:
+    """(output bits, internal bits) of one IR op consuming tensors of the given widths."""
+    import json as _json
+    text = _json.dumps(op).encode()
+    arr = (C.c_int * max(len(input_bits), 1))(*input_bits)
+    out, internal = C.c_int(), C.c_int()
+    _check("pnb_op_bits", lib().pnb_op_bits(text, len(text), arr, len(input_bits),
+                                            C.byref(out), C.byref(internal)))
+    return out.value, internal.value
 
 
 def wait_probe(device: int = 0, polls: int = 1000) -> int:

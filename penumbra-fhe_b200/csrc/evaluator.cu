@@ -331,6 +331,23 @@ int pnb_graph_check_budget(const pnb_graph* g) {
   }
 }
 
+int pnb_op_bits(const char* op_json, size_t len, const int* input_bits, int n_inputs,
+                int* output_bits, int* internal_bits) {
+  if (!op_json || (!input_bits && n_inputs > 0) || n_inputs < 0 || !output_bits ||
+      !internal_bits) {
+    set_error("pnb_op_bits: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  try {
+    ir::op_bits(op_json, len, std::vector<int>(input_bits, input_bits + n_inputs), output_bits,
+                internal_bits);
+    return PNB_OK;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
 int pnb_plan_create(const pnb_graph* g, const pnb_params* p, const int64_t* input_lens,
                     int64_t input_lo, int64_t input_hi, double margin_sigmas, pnb_plan** out) {
   if (!g || !p || !out) {

@@ -236,6 +236,20 @@ int op_internal_bits(const OpSpec& op, const std::vector<int>& in_bits) {
 
 }  // namespace
 
+void op_bits(const char* op_json, size_t len, const std::vector<int>& in_bits, int* output_bits,
+             int* internal_bits) {
+  Value v;
+  try {
+    v = json::parse(op_json, len);
+  } catch (const std::exception& e) {
+    bad(std::string("IR parse error: ") + e.what());
+  }
+  const OpSpec op = parse_op(v);
+  validate_op(op);
+  *output_bits = op_output_bits(op, in_bits);
+  *internal_bits = op_internal_bits(op, in_bits);
+}
+
 void validate_op(const OpSpec& op) {
   switch (op.type) {
     case OpType::Linear: {

@@ -76,6 +76,12 @@ void validate_op(const OpSpec& op);
 std::unordered_map<std::string, int> propagate_bit_widths(const Graph& g);
 void check_graph_bit_width_budget(const Graph& g);
 
+// Output and internal bit widths of one op payload (JSON object) given its input widths: the
+// per-op rules of Op::output_bits_n / Op::internal_bits_n (runtime/src/ops/mod.rs:77-138),
+// after the op's validation.
+void op_bits(const char* op_json, size_t len, const std::vector<int>& in_bits, int* output_bits,
+             int* internal_bits);
+
 // Flat output length of an op given its input lengths (the shape rule each op's eval asserts).
 int64_t output_length(const OpSpec& op, const std::vector<int64_t>& in_lens);
 

@@ -174,5 +174,19 @@ def main():
         print(f"ref_{name}: {len(outs)} samples, {key} reproduced -> {os.path.relpath(path)}")
 
 
+def copy_bitwidth_cases():
+    """The reference's cross-language bit-width conformance table (tests/fixtures/
+    bitwidth_cases.json), copied unchanged for tests/test_graph_cpu.py."""
+    src = os.path.join(REF, "tests", "fixtures", "bitwidth_cases.json")
+    dst_dir = os.path.join(HERE, "conformance")
+    os.makedirs(dst_dir, exist_ok=True)
+    with open(src) as f:
+        doc = json.load(f)
+    with open(os.path.join(dst_dir, "ref_bitwidth_cases.json"), "w") as f:
+        json.dump(doc, f, indent=1)
+    print(f"ref_bitwidth_cases: {len(doc['cases'])} cases")
+
+
 if __name__ == "__main__":
     main()
+    copy_bitwidth_cases()

@@ -163,3 +163,19 @@ def test_bit_width_budget(pnb):
         g.check_budget()
     with pytest.raises(pnb.LibraryError, match="bit-width budget exceeded"):
         pnb.Plan(g)
+
+
+def _bitwidth_cases():
+    with open(os.path.join(GOLDEN_DIR, "conformance", "ref_bitwidth_cases.json")) as f:
+        return json.load(f)["cases"]
+
+
+@pytest.mark.parametrize("case", _bitwidth_cases(), ids=lambda c: c["name"])
+def test_bitwidth_conformance_table(pnb, case):
+    # The reference's cross-language table (tests/fixtures/bitwidth_cases.json, checked there
+    # by runtime/tests/bitwidth_conformance.rs and tests/test_bitwidth_conformance.py): every
+    # op's output width, and the Requant's internal width, must be reproduced exactly.
+    out, internal = pnb.op_bits(case["op"], case["input_bits"])
+    assert out == case["expected"]
+    if "expected_internal" in case:
+        assert internal == case["expected_internal"]
