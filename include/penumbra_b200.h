@@ -63,6 +63,15 @@ int pnb_params_default(pnb_params* out);
  * on `device` from `seed`; blocks until the keys are resident.
  * Replaces: keys::keygen -> tfhe gen_keys_radix (runtime/src/keys.rs:47-56). */
 int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** out);
+/* Build a key set on `device` from key material on the host, in pnb_keys_export's layouts:
+ * bsk (standard domain) and ksk are required; lwe_sk and glwe_sk are both given or both NULL.
+ * Without them the set is an evaluation-key set (the server's view): bootstraps, keyswitches
+ * and graph evaluation work, encryption and phases are refused.  The Fourier bootstrapping key
+ * is computed on the device.  Blocking.  Replaces: deserialising a ServerKey / uploading the
+ * client's evaluation keys (the keys the reference's keys::keygen returns, keys.rs:47-56). */
+int pnb_keys_import(int device, const pnb_params* params, const uint64_t* lwe_sk_host,
+                    const uint64_t* glwe_sk_host, const uint64_t* bsk_host,
+                    const uint64_t* ksk_host, pnb_keys** out);
 int pnb_keys_free(pnb_keys* keys);
 int pnb_keys_info(const pnb_keys* keys, pnb_params* params_out, int* device_out,
                   size_t* fourier_bsk_bytes, size_t* ksk_bytes);

@@ -21,7 +21,7 @@ __all__ = [
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
-    "gather_shards", "evaluate_sharded", "op_bits", "wait_probe",
+    "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -60,6 +60,8 @@ _SIGS = {
     "pnb_params_default": (C.c_int, [C.POINTER(Params)]),
     "pnb_keygen": (C.c_int, [C.c_int, C.POINTER(Params), C.c_uint64, C.POINTER(C.c_void_p)]),
     "pnb_keys_free": (C.c_int, [C.c_void_p]),
+    "pnb_keys_import": (C.c_int, [C.c_int, C.POINTER(Params), C.c_void_p, C.c_void_p,
+                                 C.c_void_p, C.c_void_p, C.POINTER(C.c_void_p)]),
     "pnb_keys_info": (C.c_int, [C.c_void_p, C.POINTER(Params), C.POINTER(C.c_int),
                                 C.POINTER(C.c_size_t), C.POINTER(C.c_size_t)]),
     "pnb_keys_export": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
@@ -229,6 +231,25 @@ def keygen(params: Params | None = None, seed: int = 0, device: int = 0) -> KeyS
     h = C.c_void_p()
     _check("pnb_keygen", lib().pnb_keygen(device, C.byref(params), seed, C.byref(h)))
     return KeySet(h, params, device, seed)
+
+
+def import_keys(params: Params, keys: dict, device: int = 0) -> KeySet:
+    """Key set from host arrays in ``KeySet.export`` layouts (``bsk`` and ``ksk`` required;
+    ``lwe_sk`` and ``glwe_sk`` optional, together).  Mirrors ``pnb_keys_import``."""
+    import numpy as np
+    bufs = []
+    for name in ("lwe_sk", "glwe_sk", "bsk", "ksk"):
+        a = keys.get(name)
+        if a is None:
+            bufs.append(C.c_void_p(0))
+        else:
+            a = np.ascontiguousarray(a, dtype=np.uint64)
+            keys = dict(keys, **{name: a})  # keep the converted array alive during the call
+            bufs.append(C.c_void_p(a.ctypes.data))
+    h = C.c_void_p()
+    _check("pnb_keys_import",
+           lib().pnb_keys_import(device, C.byref(params), *bufs, C.byref(h)))
+    return KeySet(h, params, device, 0)
 
 
 def _u64(t: torch.Tensor) -> torch.Tensor:

@@ -72,6 +72,34 @@ static int check_keys(const pnb_keys* K) {
   return PNB_OK;
 }
 
+// Client-side operations need the secret keys, which an imported evaluation-key set may lack.
+static int check_secret(const pnb_keys* K, bool small) {
+  if (small ? !K->lwe_sk : !K->glwe_sk) {
+    set_error("this key set holds no %s secret key (evaluation keys imported without it)",
+              small ? "small" : "big");
+    return PNB_ERR_INVALID;
+  }
+  return PNB_OK;
+}
+
+// Device buffers of a key set for `p` (secret keys only when asked for).
+static int alloc_keys(pnb_keys* K, const pnb_params& p, bool with_secrets) {
+  const size_t rows = (size_t)(p.k + 1) * p.pbs_level;
+  K->bsk_words = (size_t)p.n * rows * (p.k + 1) * p.N;
+  K->fbsk_elems = K->bsk_words / 2;
+  K->ksk_row = (p.n + 2) & ~1;
+  K->ksk_words = (size_t)p.k * p.N * p.ks_level * K->ksk_row;
+  cudaError_t e = cudaSuccess;
+  if ((with_secrets && ((e = cudaMalloc(&K->lwe_sk, sizeof(uint64_t) * p.n)) != cudaSuccess ||
+                        (e = cudaMalloc(&K->glwe_sk, sizeof(uint64_t) * p.k * p.N)) !=
+                            cudaSuccess)) ||
+      (e = cudaMalloc(&K->bsk, sizeof(uint64_t) * K->bsk_words)) != cudaSuccess ||
+      (e = cudaMalloc(&K->fbsk, sizeof(double2) * K->fbsk_elems)) != cudaSuccess ||
+      (e = cudaMalloc(&K->ksk, sizeof(uint64_t) * K->ksk_words)) != cudaSuccess)
+    return cuda_status(e, "cudaMalloc(keys)");
+  return PNB_OK;
+}
+
 }  // namespace pnb
 
 using namespace pnb;
@@ -112,21 +140,12 @@ int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** o
   K->p = *params;
   K->seed = seed;
   const pnb_params& p = *params;
-  const size_t rows = (size_t)(p.k + 1) * p.pbs_level;
-  K->bsk_words = (size_t)p.n * rows * (p.k + 1) * p.N;
-  K->fbsk_elems = K->bsk_words / 2;
-  K->ksk_row = (p.n + 2) & ~1;
-  K->ksk_words = (size_t)p.k * p.N * p.ks_level * K->ksk_row;
-  cudaError_t e;
-  if ((e = cudaMalloc(&K->lwe_sk, sizeof(uint64_t) * p.n)) != cudaSuccess ||
-      (e = cudaMalloc(&K->glwe_sk, sizeof(uint64_t) * p.k * p.N)) != cudaSuccess ||
-      (e = cudaMalloc(&K->bsk, sizeof(uint64_t) * K->bsk_words)) != cudaSuccess ||
-      (e = cudaMalloc(&K->fbsk, sizeof(double2) * K->fbsk_elems)) != cudaSuccess ||
-      (e = cudaMalloc(&K->ksk, sizeof(uint64_t) * K->ksk_words)) != cudaSuccess) {
-    rc = cuda_status(e, "cudaMalloc(keys)");
+  rc = alloc_keys(K, p, true);
+  if (rc) {
     pnb_keys_free(K);
     return rc;
   }
+  cudaError_t e;
   cudaStream_t st = 0;
   rc = keygen_device(K, st);
   if (rc == PNB_OK && p.N == 2048) {
@@ -137,6 +156,65 @@ int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** o
     if (e != cudaSuccess) rc = cuda_status(e, "keygen synchronize");
   }
   if (rc) { pnb_keys_free(K); return rc; }
+  *out = K;
+  return PNB_OK;
+}
+
+int pnb_keys_import(int device, const pnb_params* params, const uint64_t* lwe_sk,
+                    const uint64_t* glwe_sk, const uint64_t* bsk, const uint64_t* ksk,
+                    pnb_keys** out) {
+  if (!out) { set_error("out is NULL"); return PNB_ERR_INVALID; }
+  *out = nullptr;
+  if (!bsk || !ksk) {
+    set_error("pnb_keys_import: the bootstrapping and keyswitching keys are required");
+    return PNB_ERR_INVALID;
+  }
+  if (!lwe_sk != !glwe_sk) {
+    set_error("pnb_keys_import: give both secret keys or neither");
+    return PNB_ERR_INVALID;
+  }
+  int rc = validate_params(params);
+  if (rc) return rc;
+  if (params->N != 2048) {
+    set_error("pnb_keys_import: the Fourier conversion is compiled for N = 2048 (got %d)",
+              params->N);
+    return PNB_ERR_UNSUPPORTED;
+  }
+  DeviceGuard g(device);
+  if (g.rc) return g.rc;
+  pnb_keys* K = new (std::nothrow) pnb_keys();
+  if (!K) { set_error("host allocation failed"); return PNB_ERR_OOM; }
+  K->device = device;
+  K->p = *params;
+  K->seed = 0;
+  const pnb_params& p = *params;
+  rc = alloc_keys(K, p, lwe_sk != nullptr);
+  cudaError_t e = cudaSuccess;
+  if (rc == PNB_OK && lwe_sk) {
+    if ((e = cudaMemcpy(K->lwe_sk, lwe_sk, 8 * (size_t)p.n, cudaMemcpyHostToDevice)) !=
+            cudaSuccess ||
+        (e = cudaMemcpy(K->glwe_sk, glwe_sk, 8 * (size_t)p.k * p.N, cudaMemcpyHostToDevice)) !=
+            cudaSuccess)
+      rc = cuda_status(e, "pnb_keys_import(secret keys)");
+  }
+  if (rc == PNB_OK &&
+      (e = cudaMemcpy(K->bsk, bsk, 8 * K->bsk_words, cudaMemcpyHostToDevice)) != cudaSuccess)
+    rc = cuda_status(e, "pnb_keys_import(bootstrapping key)");
+  if (rc == PNB_OK) {
+    // rows of n+1 words on the host, padded to ksk_row words on the device (pad words zero)
+    const size_t rows = (size_t)p.k * p.N * p.ks_level;
+    if ((e = cudaMemset(K->ksk, 0, 8 * K->ksk_words)) != cudaSuccess ||
+        (e = cudaMemcpy2D(K->ksk, 8 * (size_t)K->ksk_row, ksk, 8 * (size_t)(p.n + 1),
+                          8 * (size_t)(p.n + 1), rows, cudaMemcpyHostToDevice)) != cudaSuccess)
+      rc = cuda_status(e, "pnb_keys_import(keyswitching key)");
+  }
+  if (rc == PNB_OK) rc = bsk_to_fourier(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), 0);
+  if (rc == PNB_OK && (e = cudaStreamSynchronize(0)) != cudaSuccess)
+    rc = cuda_status(e, "pnb_keys_import synchronize");
+  if (rc) {
+    pnb_keys_free(K);
+    return rc;
+  }
   *out = K;
   return PNB_OK;
 }
@@ -171,6 +249,7 @@ int pnb_keys_export(const pnb_keys* K, uint64_t* lwe_sk, uint64_t* glwe_sk, uint
   DeviceGuard g(K->device);
   if (g.rc) return g.rc;
   const pnb_params& p = K->p;
+  if ((lwe_sk || glwe_sk) && (rc = check_secret(K, false))) return rc;
   if (lwe_sk) PNB_CUDA(cudaMemcpy(lwe_sk, K->lwe_sk, 8 * p.n, cudaMemcpyDeviceToHost));
   if (glwe_sk)
     PNB_CUDA(cudaMemcpy(glwe_sk, K->glwe_sk, 8 * (size_t)p.k * p.N, cudaMemcpyDeviceToHost));
@@ -192,6 +271,7 @@ int pnb_encrypt_lwe(const pnb_keys* K, const int64_t* messages_dev, uint64_t del
     set_error("encrypt: bad buffers or count %d", count);
     return PNB_ERR_INVALID;
   }
+  if ((rc = check_secret(K, false))) return rc;
   DeviceGuard g(K->device);
   if (g.rc) return g.rc;
   return encrypt_lwe(K, messages_dev, delta, seed, first_index, ct_dev, count,
@@ -206,6 +286,7 @@ int pnb_phase_lwe(const pnb_keys* K, const uint64_t* ct_dev, uint64_t* phase_dev
     set_error("phase: bad buffers or count %d", count);
     return PNB_ERR_INVALID;
   }
+  if ((rc = check_secret(K, small_key != 0))) return rc;
   DeviceGuard g(K->device);
   if (g.rc) return g.rc;
   return phase_lwe(K, ct_dev, phase_dev, count, small_key, (cudaStream_t)stream);

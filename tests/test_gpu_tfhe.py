@@ -203,3 +203,23 @@ def test_bounded_wait_gives_up_and_context_survives(pnb, gkeys):
     out = pnb.pbs_batch(gkeys, tv, pnb.encrypt(gkeys, torch.tensor(msgs), seed=3))
     assert np.array_equal(pnb.decrypt_vec(gkeys, out).cpu().numpy(), np.array(lut)[msgs])
     assert pnb.device_status(0) == 0
+
+
+def test_imported_evaluation_keys_bootstrap_identically(pnb, gkeys):
+    """Evaluation keys exported to the host and imported without the secret keys (the server's
+    view) bootstrap bit-identically to the generating key set; the secret-less set refuses
+    client-side operations, and an import with the secrets restores them."""
+    ex = gkeys.export(lwe_sk=True, glwe_sk=True, bsk=True, ksk=True)
+    server = pnb.import_keys(gkeys.params, {"bsk": ex["bsk"], "ksk": ex["ksk"]}, device=0)
+    lut = [(5 * v + 3) % 16 for v in range(16)]
+    msgs = np.arange(256) % 16
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=9)
+    want = pnb.pbs_batch(gkeys, pnb.test_vector(gkeys, lut), ct)
+    got = pnb.pbs_batch(server, pnb.test_vector(server, lut), ct)
+    assert torch.equal(got, want)
+    assert np.array_equal(pnb.decrypt_vec(gkeys, got).cpu().numpy(), np.array(lut)[msgs])
+    with pytest.raises(pnb.LibraryError, match="no big secret key"):
+        pnb.encrypt(server, torch.tensor(msgs), seed=1)
+    full = pnb.import_keys(gkeys.params, ex, device=0)
+    assert torch.equal(pnb.encrypt(full, torch.tensor(msgs), seed=9), ct)
+    assert pnb.device_status(0) == 0
