@@ -135,7 +135,8 @@ int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* 
  * ciphertexts and larger counts are rejected with PNB_ERR_INVALID (split the batch).  The
  * first call on a device looks up that array's device address; make that first call before
  * any stream capture.  Calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  The key set must come from pnb_keygen on the same device.
+ * serialised by the caller.  The key set must come from pnb_keygen or pnb_keys_import on the
+ * same device.
  * No counterpart in the reference. */
 int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
                           uint64_t* out_dev, int count, void* stream);

@@ -57,7 +57,7 @@ int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in,
   }
   if (!fft_tables_ready()) {
     set_error("pbs_noalloc: the FFT tables of this device are not built; create the key set "
-              "with pnb_keygen on this device first");
+              "with pnb_keygen or pnb_keys_import on this device first");
     return PNB_ERR_INVALID;
   }
   int dev = 0;
