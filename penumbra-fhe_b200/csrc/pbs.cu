@@ -462,16 +462,23 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   const double2* och = reinterpret_cast<const double2*>(reinterpret_cast<double*>(mlb_raw) +
                                                         (warp ^ 1) * FFT_M);
   // accumulator word t = hi[t] 2^32 + lo[t] 2^16 (the low 16 bits stay zero)
-  // with coefficients (j, j + M) side by side: hi2[j] = (hi[j], hi[j + M]), lo2 likewise
+  // with coefficients (j, j + M) side by side: hi2[j] = (hi[j], hi[j + M]), lo2 likewise.
+  // A32: when the digits read at most 30 bits (beta L <= 30) only hi is kept -- the top 32 bits,
+  // as in the single-level kernel (the dropped word adds a random walk of ~2^36 against these
+  // key sets' 2^41 and more of output noise).
+  constexpr bool A32 = BETA > 0 && BETA * L <= 30;
   uint2* hi2 = reinterpret_cast<uint2*>(mlb_raw + Y::OFF_HI) + warp * FFT_M;
   ushort2* lo2 = reinterpret_cast<ushort2*>(mlb_raw + Y::OFF_LO) + warp * FFT_M;
-  auto word = [](uint32_t hi, uint16_t lo) { return ((uint64_t)hi << 32) | ((uint64_t)lo << 16); };
+  auto word = [](uint32_t hi, uint16_t lo) {
+    return ((uint64_t)hi << 32) | (A32 ? 0ull : (uint64_t)lo << 16);
+  };
   auto acc_at = [&](int e) {
-    return e < FFT_M ? word(hi2[e].x, lo2[e].x) : word(hi2[e - FFT_M].y, lo2[e - FFT_M].y);
+    return e < FFT_M ? word(hi2[e].x, A32 ? 0 : lo2[e].x)
+                     : word(hi2[e - FFT_M].y, A32 ? 0 : lo2[e - FFT_M].y);
   };
   auto acc_put2 = [&](int k, uint64_t v0, uint64_t v1) {
     hi2[k] = make_uint2((uint32_t)(v0 >> 32), (uint32_t)(v1 >> 32));
-    lo2[k] = make_ushort2((uint16_t)(v0 >> 16), (uint16_t)(v1 >> 16));
+    if (!A32) lo2[k] = make_ushort2((uint16_t)(v0 >> 16), (uint16_t)(v1 >> 16));
   };
   const double2* ggsw_s = reinterpret_cast<const double2*>(mlb_raw + Y::OFF_GGSW);
   const uint32_t bar = tc::smem_u32(mlb_raw + Y::OFF_BAR);
@@ -494,8 +501,14 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   const uint64_t* tv = tv_of(sel, valid ? ct : 0);
   const int bt = valid ? modswitch(in[n], LG) : 0;
   const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
-  for (int t = lane; t < FFT_M; t += 32)
-    acc_put2(t, (p == 0) ? 0 : rot_coef(tv, t, r0), (p == 0) ? 0 : rot_coef(tv, t + FFT_M, r0));
+  for (int t = lane; t < FFT_M; t += 32) {
+    // A32 keeps the rounded top word (as the single-level kernel does)
+    auto init = [&](int e) {
+      const uint64_t v = (p == 0) ? 0 : rot_coef(tv, e, r0);
+      return A32 ? (v + 0x80000000ull) & ~0xffffffffull : v;
+    };
+    acc_put2(t, init(t), init(t + FFT_M));
+  }
   uint64_t a_next = valid ? in[0] : 0;  // mask coefficient of the next CMux, loaded one ahead
   __syncthreads();
 
@@ -516,6 +529,10 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   const uint64_t vk_off = (1ull << (63 - beta * L)) + (hsum << (64 - beta * L));
   const uint32_t dmask = (1u << beta) - 1u;
   const int dhalf = 1 << (beta - 1);
+  // A32: the digit source is the top word; the rounding unit is bit 32 - T of it, and ties are
+  // broken to even by adding half a unit less one plus the lowest kept bit
+  const int rnd_sh = A32 ? 32 - beta * L : 1;
+  const uint32_t off_h = A32 ? (uint32_t)(vk_off >> 32) - 1u : 0u;
   uint32_t stage = 0;
   bool aborted = false;
 
@@ -539,18 +556,33 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
           // reads (x, y) as they are, -M <= t < 0 reads (-y, x), t < -M reads (-x, -y)
           const int tr = j - ar;
           const uint2 gh = hi2[tr & (FFT_M - 1)], oh = hi2[j];
-          const ushort2 gl = lo2[tr & (FFT_M - 1)], ol = lo2[j];
           const bool sw = (unsigned)(tr + FFT_M) < (unsigned)FFT_M;
-          const uint64_t n0 = (tr < 0 ? ~0ull : 0ull) ^ flip;
-          const uint64_t n1 = (tr < -FFT_M ? ~0ull : 0ull) ^ flip;
-          const uint64_t ga = word(gh.x, gl.x), gb = word(gh.y, gl.y);
-          const uint64_t g0 = sw ? gb : ga, g1 = sw ? ga : gb;
-          const uint64_t v0 = ((g0 ^ n0) - n0) - word(oh.x, ol.x) + vk_off;
-          const uint64_t v1 = ((g1 ^ n1) - n1) - word(oh.y, ol.y) + vk_off;
-          t[4 * q + 0] = (uint32_t)v0;
-          t[4 * q + 1] = (uint32_t)(v0 >> 32);
-          t[4 * q + 2] = (uint32_t)v1;
-          t[4 * q + 3] = (uint32_t)(v1 >> 32);
+          if (A32) {
+            // The same in 32-bit words, vk in the top word.  With no bits below the word,
+            // exact ties of the rounding (v mod 2^(33-T+32) = half a unit) are common, and
+            // rounding them all up would bias every coefficient by half a word -- a bias the
+            // external product sums coherently over the key.  Ties go to the even value.
+            const uint32_t f32 = (uint32_t)flip;
+            const uint32_t n0 = (tr < 0 ? ~0u : 0u) ^ f32, n1 = (tr < -FFT_M ? ~0u : 0u) ^ f32;
+            const uint32_t g0 = sw ? gh.y : gh.x, g1 = sw ? gh.x : gh.y;
+            const uint32_t w0 = ((g0 ^ n0) - n0) - oh.x, w1 = ((g1 ^ n1) - n1) - oh.y;
+            t[4 * q + 0] = 0u;
+            t[4 * q + 1] = w0 + off_h + ((w0 >> rnd_sh) & 1u);
+            t[4 * q + 2] = 0u;
+            t[4 * q + 3] = w1 + off_h + ((w1 >> rnd_sh) & 1u);
+          } else {
+            const ushort2 gl = lo2[tr & (FFT_M - 1)], ol = lo2[j];
+            const uint64_t n0 = (tr < 0 ? ~0ull : 0ull) ^ flip;
+            const uint64_t n1 = (tr < -FFT_M ? ~0ull : 0ull) ^ flip;
+            const uint64_t ga = word(gh.x, gl.x), gb = word(gh.y, gl.y);
+            const uint64_t g0 = sw ? gb : ga, g1 = sw ? ga : gb;
+            const uint64_t v0 = ((g0 ^ n0) - n0) - word(oh.x, ol.x) + vk_off;
+            const uint64_t v1 = ((g1 ^ n1) - n1) - word(oh.y, ol.y) + vk_off;
+            t[4 * q + 0] = (uint32_t)v0;
+            t[4 * q + 1] = (uint32_t)(v0 >> 32);
+            t[4 * q + 2] = (uint32_t)v1;
+            t[4 * q + 3] = (uint32_t)(v1 >> 32);
+          }
         }
         tc::tmem_st_32x32_x16(tvk + (uint32_t)(16 * g), t);
       }
@@ -636,15 +668,22 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
       }
     }
     if (aborted) break;
-    fft_inverse_h<PNB_ML_CBANK, 10 + 16>(x, buf, lane, tb.wi);
+    fft_inverse_h<PNB_ML_CBANK, A32 ? 10 + 32 : 10 + 16>(x, buf, lane, tb.wi);
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
-      const uint2 h = hi2[j];
-      const ushort2 l = lo2[j];
-      acc_put2(j, word(h.x, l.x) + scaled_f64_to_top48(x[m].x),
-               word(h.y, l.y) + scaled_f64_to_top48(x[m].y));
+      if (A32) {
+        uint2 h = hi2[j];
+        h.x += scaled_f64_to_top32(x[m].x);
+        h.y += scaled_f64_to_top32(x[m].y);
+        hi2[j] = h;
+      } else {
+        const uint2 h = hi2[j];
+        const ushort2 l = lo2[j];
+        acc_put2(j, word(h.x, l.x) + scaled_f64_to_top48(x[m].x),
+                 word(h.y, l.y) + scaled_f64_to_top48(x[m].y));
+      }
     }
     __syncwarp();
   }
