@@ -210,7 +210,7 @@ def contraction_leg(args, pnb, local, dev, flush):
     macs = M * K * B * L
     return {
         "metric": "contraction_u64_macs_per_second", "value": macs / (avg * 1e-3),
-        "unit": "u64 MAC/s", "ms": avg,
+        "unit": "u64 MAC/s", "ms": avg, "ms_median": statistics.median(ms), "ms_min": min(ms),
         "config": {"workload": f"Linear {K}->{M}, int4 weights U[-8,7], {B} samples of {K} "
                                f"ciphertexts (kN+1 = {L} words)",
                    "l2": "inputs (%.2f GB) exceed L2; flushed between steps" %
