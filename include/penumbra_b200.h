@@ -141,6 +141,20 @@ int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* 
 int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
                           uint64_t* out_dev, int count, void* stream);
 
+/* Merge radix integers into wide ciphertexts.  blocks_dev is [count][num_blocks][k*N+1]: one
+ * integer per row, block 0 least significant, each block a big-key ciphertext of one digit
+ * (msg_bits bits plus carries, delta 2^(63 - msg_bits - carry_bits)), as the reference encrypts
+ * a signed radix integer.  out_dev [count][k*N+1] receives each integer v as v * delta_out
+ * (mod 2^64).  With is_signed the top block's digit is read as two's complement and carries
+ * above it are dropped.  Costs one bootstrap per block plus one sum.  The noise is the sum of
+ * num_blocks bootstrap outputs, so decryption needs delta_out well above that noise and
+ * |v| * delta_out < 2^62.  Requires num_blocks * msg_bits <= 63.
+ * Replaces: RadixClientKey::encrypt_signed / decrypt_signed's block encoding at a graph
+ * boundary (runtime/src/encrypt.rs:20-22, 43-45): ciphertexts in the reference's radix form
+ * enter the wide-ciphertext kernels. */
+int pnb_radix_merge(const pnb_keys* keys, const uint64_t* blocks_dev, int num_blocks, int count,
+                    int is_signed, uint64_t delta_out, uint64_t* out_dev, void* stream);
+
 /* Ciphertext x cleartext-weight contraction over LWE vectors mod 2^64, on the tensor cores:
  *   Y[b][j][c] = sum_i W[j][i] * X[b][i][c]  + (c == lwe_len-1 ? bias[j]*delta : 0)
  * W is int8 row-major [M][K] (K <= 65536), bias int64 [M] (may be NULL), X [batch][K][lwe_len],

@@ -21,7 +21,7 @@ __all__ = [
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
-    "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys",
+    "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys", "radix_merge",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -81,6 +81,8 @@ _SIGS = {
                                 C.c_void_p, C.c_size_t, C.c_void_p]),
     "pnb_pbs_batch_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                         C.c_void_p]),
+    "pnb_radix_merge": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_uint64,
+                                  C.c_void_p, C.c_void_p]),
     "pnb_lwe_contract_gather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
                                           C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                                           C.c_void_p]),
@@ -380,6 +382,23 @@ def pbs_batch_noalloc(keys: KeySet, tv: torch.Tensor, ct: torch.Tensor,
     _check("pnb_pbs_batch_noalloc",
            lib().pnb_pbs_batch_noalloc(keys.handle, _ptr(tv), _ptr(ct), _ptr(out), count,
                                        _stream(ct.device)))
+    return out
+
+
+def radix_merge(keys: KeySet, blocks: torch.Tensor, delta_out: int, signed: bool = True,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Merge radix integers ``blocks[count, num_blocks, kN+1]`` (block 0 least significant, one
+    digit per block at the reference's block delta) into wide ciphertexts ``[count, kN+1]``
+    encrypting each integer times ``delta_out``: one bootstrap per block, then a sum."""
+    blocks = _u64(blocks).contiguous()
+    count, nb, L = blocks.shape
+    if L != keys.big_dim + 1:
+        raise ValueError(f"blocks have {L} words, the key set's ciphertexts {keys.big_dim + 1}")
+    if out is None:
+        out = torch.empty((count, L), dtype=torch.int64, device=blocks.device)
+    _check("pnb_radix_merge",
+           lib().pnb_radix_merge(keys.handle, _ptr(blocks), nb, count, int(bool(signed)),
+                                 delta_out % (1 << 64), _ptr(out), _stream(blocks.device)))
     return out
 
 

@@ -380,6 +380,20 @@ int pnb_pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv_dev, const uint6
   return pbs_batch_noalloc(K, tv_dev, in_dev, out_dev, count, (cudaStream_t)stream);
 }
 
+int pnb_radix_merge(const pnb_keys* K, const uint64_t* blocks_dev, int num_blocks, int count,
+                    int is_signed, uint64_t delta_out, uint64_t* out_dev, void* stream) {
+  int rc = check_keys(K);
+  if (rc) return rc;
+  if (count < 0 || (count > 0 && (!blocks_dev || !out_dev))) {
+    set_error("radix_merge: bad buffers or count %d", count);
+    return PNB_ERR_INVALID;
+  }
+  DeviceGuard g(K->device);
+  if (g.rc) return g.rc;
+  return radix_merge(K, blocks_dev, num_blocks, count, is_signed != 0, delta_out, out_dev,
+                     (cudaStream_t)stream);
+}
+
 int pnb_lwe_contract(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M, int K,
                      const uint64_t* X_dev, uint64_t* Y_dev, int batch, int lwe_len,
                      void* stream) {

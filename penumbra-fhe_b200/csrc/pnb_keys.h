@@ -36,6 +36,10 @@ int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_
               int count, void* ws, size_t ws_bytes, cudaStream_t st);
 int test_vector(const pnb_keys* K, const uint64_t* lut_host, int lut_len, uint64_t delta_out,
                 uint64_t* tv, cudaStream_t st);
+// Merge [count][nb] radix-block ciphertexts into [count] wide ciphertexts (radix.cu).
+int radix_merge(const pnb_keys* K, const uint64_t* blocks, int nb, int count, bool is_signed,
+                uint64_t delta_out, uint64_t* out, cudaStream_t st);
+void radix_merge_lut(int msg_bits, int carry_bits, int nb, int i, bool is_signed, uint64_t* lut);
 int fft_negacyclic_mul(int N, const int64_t* a, const uint64_t* b, uint64_t* out, int count,
                        cudaStream_t st);
 int encrypt_lwe(const pnb_keys* K, const int64_t* msg, uint64_t delta, uint64_t seed,
