@@ -11,20 +11,29 @@ runtime/src/ops/activation.rs:115).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl reference]
 
-Second workload, reported under "mlp" in the same line: the 6-bit MLP 784-128-128-10 (graph
-quantized by the reference quantizer, tests/golden/cfg4_mlp.json) evaluated end to end under
-encryption -- the whole graph, every Linear on the tensor cores and every Requant as an exact
-bootstrap program -- on `--mlp-batch` synthetic samples per GPU (seeded uniform 6-bit inputs).
+Per-configuration legs, at the end of the same line (the driver keeps the line's tail):
+  "mlp"  -- configuration 4: the 6-bit MLP 784-128-128-10 (graph quantized by the reference
+            quantizer, tests/golden/cfg4_mlp.json) evaluated end to end under encryption --
+            every Linear on the tensor cores, every Requant an exact bootstrap program -- on a
+            fixed global batch of `--mlp-batch` (1024) synthetic samples sharded over the GPUs
+            (strong scaling);
+  "cnn"  -- configuration 5: the small CNN (tests/golden/cfg5_cnn.json) on `--cnn-batch` (64)
+            samples per GPU, so 8 GPUs evaluate the configuration's 512-sample batch;
+  "linear_requant" -- configuration 3's Linear 784->128 + ReLU-Requant (N=2048 set);
+  "contraction"    -- the encrypted Linear 784->128 (int4 weights, 256 samples of 784
+                      ciphertexts) on the tensor cores against the HBM roofline;
+  "noise"          -- the single-level bootstrap's output noise over ~1e5 bootstraps beside its
+                      analytic value and the CPU restatements' (95% intervals);
+  "pbs_by_key_set", "pbs_batch_sweep" -- PBS/s of the multi-level key sets, and across batch
+                      sizes 1 to 65536.
+Every graph leg decrypts every sample on rank 0 and compares it with the cleartext graph.
 
-Also in the line: "pbs_batch_sweep" -- PBS/s at batch sizes 1 to 65536; "contraction" -- the encrypted Linear 784->128 (int4 weights, 256 samples of
-784 ciphertexts) on the tensor cores against the HBM roofline; "noise" -- the single-level
-bootstrap's output noise over ~1e5 bootstraps beside its analytic value.
-
-N > 1 runs one process per GPU under torchrun; each rank bootstraps its own batch against
-its own key replica (weak scaling, no data-path collective), time = max over ranks.  The MLP
-shards samples over ranks and reassembles the output ciphertexts with one NCCL all-gather.
-`--impl reference` times the CPU restatement of the same PBS (the oracle's f64 FFT path, the
-algorithm tfhe-rs runs on the CPU) on all host cores; it needs no GPU.
+N > 1 runs one process per GPU under torchrun; in the PBS leg each rank bootstraps its own 4096
+ciphertexts against its own key replica and one NCCL all-gather per step reassembles the
+layer's outputs on every rank (weak scaling), time = max over ranks.  The graph legs shard
+samples over ranks and reassemble the output ciphertexts with one NCCL all-gather.
+`--impl reference` times the CPU restatement of the same PBS (the oracle's unvectorised f64 FFT
+path, the algorithm tfhe-rs runs on the CPU) on all host cores; it needs no GPU.
 """
 from __future__ import annotations
 
@@ -126,6 +135,14 @@ def dist_setup(args):
     return world, rank, local
 
 
+def pbs_config(batch: int, world: int) -> dict:
+    """The PBS microbenchmark's `config` (both arms print the same one)."""
+    return {"workload": WORKLOAD, "batch_per_gpu": batch, "global_batch": batch * world,
+            "parallelism": (f"ciphertexts sharded over {world} GPUs, outputs all-gathered over "
+                            "NCCL every step" if world > 1 else "one GPU"),
+            "l2": "flushed (256 MB write) between timed steps"}
+
+
 def cpu_reference_run(args, samples_per_step: int, warmup: int, steps: int):
     """Time the oracle's f64-FFT PBS on all host cores; returns (PBS/s, info)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -164,11 +181,12 @@ def run_reference(args):
         "n_gpus": args.gpus, "steps": steps, "warmup": warm,
         "ms_per_step": 1e3 * per_step / v, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "batch": per_step,
-                   "note": "each step bootstraps a bounded sample of the 4096-ciphertext batch"},
+        "config": pbs_config(args.batch, args.gpus),
         "cpu_baseline": {"value": v, "unit": "PBS/s", "cores": info["threads"], "kind": "port",
-                         "sample": f"{per_step} PBS per step x {steps} steps on "
-                                   f"{info['threads']} host threads (oracle f64-FFT PBS)"},
+                         "sample": f"each step bootstraps a bounded sample of {per_step} of the "
+                                   f"batch's ciphertexts, x {steps} steps, on {info['threads']} "
+                                   "host threads (the oracle's unvectorised f64-FFT PBS "
+                                   "restatement; tfhe-rs itself cannot be built here)"},
         "e2e": {"value": v, "unit": "PBS/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "decrypt_ok": info["decrypt_ok"],
     }
@@ -237,7 +255,8 @@ def _measured_hbm():
 
 
 def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 65536)):
-    """PBS/s (keyswitch + blind rotation, device-timed, inputs resident) across batch sizes."""
+    """[batch, PBS/s] (keyswitch + blind rotation, device-timed, inputs resident) across batch
+    sizes."""
     import numpy as np
     import torch
     rng = np.random.default_rng(SEED + 21)
@@ -263,7 +282,7 @@ def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 6
             torch.cuda.synchronize(dev)
             ms += a.elapsed_time(b)
         ms /= reps
-        out.append({"batch": B, "pbs_per_second": B / (ms * 1e-3), "ms": ms})
+        out.append([B, round(B / (ms * 1e-3))])
         del ct, small, ks_ws, o
     return out
 
@@ -304,24 +323,60 @@ def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6)), B=409
             torch.cuda.synchronize(dev)
             ms += a.elapsed_time(b)
         ms /= reps
-        out.append({"base_log": base_log, "levels": levels, "batch": B,
-                    "pbs_per_second": B / (ms * 1e-3), "decrypt_ok": ok,
-                    "log2_noise_std": log2_std})
+        out.append({"key": [base_log, levels], "pbs_per_second": round(B / (ms * 1e-3)),
+                    "decrypt_ok": ok, "log2_noise_std": round(log2_std, 3)})
         del ct, small, ks_ws, o
         keys.free()
     return out
 
 
-def noise_leg(pnb, keys, dev, total=100352):
-    """Output noise of the single-level bootstrap over ~1e5 bootstraps (phase - LUT*delta)."""
+def _ratio_ci(a, b, reps=2000, seed=0):
+    """Variance ratio var(a)/var(b) of paired error samples with a 95% percentile interval from
+    resampling the pairs."""
+    import numpy as np
+    rng = np.random.default_rng(seed)
+    n = a.size
+    r = []
+    for _ in range(reps):
+        i = rng.integers(0, n, n)
+        r.append(a[i].var() / b[i].var())
+    lo, hi = np.percentile(r, [2.5, 97.5])
+    return [float(a.var() / b.var()), float(lo), float(hi)]
+
+
+def fft_product_error(pnb, dev, base_log, polys=256):
+    """Variance of the f64-FFT negacyclic product's error per coefficient: random balanced
+    digits of the gadget (|d| <= 2^(base_log-1)) times uniform torus polynomials through the
+    blind rotation's transform (pnb_fft_negacyclic_mul), against the exact product mod 2^64."""
+    import numpy as np
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    rng = np.random.default_rng(SEED + 41)
+    N = 2048
+    h = 1 << (base_log - 1)
+    a = rng.integers(-h, h, (polys, N), dtype=np.int64)
+    b = rng.integers(0, 1 << 64, (polys, N), dtype=np.uint64)
+    got = pnb.fft_negacyclic_mul(torch.tensor(a, device=dev),
+                                 torch.tensor(b.view(np.int64), device=dev))
+    got = got.cpu().numpy().view(np.uint64)
+    want = np.stack([O.negacyclic_mul(a[i].view(np.uint64), b[i]) for i in range(polys)])
+    e = (got - want).view(np.int64).astype(np.float64)
+    return float(e.var())
+
+
+def noise_leg(pnb, keys, dev, cpu_count=8192, exact_count=512, total=100352):
+    """Output noise of the single-level bootstrap over ~1e5 bootstraps (phase - LUT*delta),
+    beside the analytic model and the CPU restatements run on the same keys and ciphertexts:
+    the f64-FFT restatement (the algorithm tfhe-rs runs) on the first `cpu_count` bootstraps
+    and the exact-arithmetic restatement (no FFT error) on the first `exact_count`."""
     import numpy as np
     import torch
     rng = np.random.default_rng(SEED + 9)
     B = 4096
     lut = rng.integers(0, 16, 16)
     tv = pnb.test_vector(keys, lut)
-    errs = []
-    first = None
+    errs, cts, ms = [], [], []
     n = 0
     while n < total:
         msgs = rng.integers(0, 16, B)
@@ -330,34 +385,54 @@ def noise_leg(pnb, keys, dev, total=100352):
         ph = pnb.phase(keys, out).cpu().numpy()
         want = (lut[msgs].astype(np.uint64) * np.uint64(keys.params.delta()))
         errs.append((ph.view(np.uint64) - want).view(np.int64).astype(np.float64))
-        if first is None:
-            first = (ct[:1024].cpu().numpy().view(np.uint64), lut, msgs[:1024])
+        if n < max(cpu_count, exact_count):
+            cts.append(ct.cpu().numpy().view(np.uint64))
+            ms.append(msgs)
         n += B
     e = np.concatenate(errs)
-    # the CPU restatement's bootstrap on the first 1024 inputs, same keys (same seed)
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle as O
-    ok = O.OracleKeys(O.default_params(), SEED)
-    cts, lut0, m0 = first
-    ref = ok.pbs_fft(cts, ok.test_vector(lut0), threads=os.cpu_count() or 1)
-    e_ref = (ok.phase_big(ref) - lut0[m0].astype(np.uint64) * np.uint64(keys.params.delta()))
-    e_ref = e_ref.view(np.int64).astype(np.float64)
-    e_gpu = e[:1024]
-    # analytic variance of the same blind rotation (key noise through the digits + gadget
-    # rounding), for comparison
     p = keys.params
+    # analytic variance: key noise through the gadget digits, gadget rounding, and the f64
+    # product's rounding error; the last two sit on the mask polynomial too, where the secret
+    # key multiplies them (1 + kN/2 terms)
     s = p.glwe_std * 2.0 ** 64
     Bb = 2.0 ** p.pbs_base_log
-    v1 = p.n * (p.k + 1) * p.pbs_level * p.N * (Bb * Bb / 12) * s * s
+    v1 = p.n * (p.k + 1) * p.pbs_level * p.N * (Bb * Bb / 12 + 1 / 6) * s * s
     eps = 2.0 ** (64 - p.pbs_base_log * p.pbs_level)
     v2 = (p.n / 2) * (1 + p.k * p.N / 2) * eps * eps / 12
-    return {"bootstraps": int(e.size), "log2_std": float(np.log2(e.std())),
-            "mean_over_std": float(e.mean() / e.std()),
-            "variance_ratio_vs_cpu_restatement": float(e_gpu.var() / e_ref.var()),
-            "cpu_restatement_log2_std": float(np.log2(e_ref.std())),
-            "ratio_sample": "first 1024 bootstraps, identical keys and ciphertexts",
-            "analytic_log2_std": float(0.5 * np.log2(v1 + v2)),
-            "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2))}
+    vprod = fft_product_error(pnb, dev, p.pbs_base_log)
+    v3 = p.n * (1 + p.k * p.N / 2) * (p.k + 1) * p.pbs_level * vprod
+    res = {"bootstraps": int(e.size), "log2_std": float(np.log2(e.std())),
+           "mean_over_std": float(e.mean() / e.std()),
+           "decrypt_errors": int(np.sum(np.abs(e) >= p.delta() / 2)),
+           "analytic_log2_std": float(0.5 * np.log2(v1 + v2 + v3)),
+           "analytic_terms_log2_std": {"key": float(0.5 * np.log2(v1)),
+                                       "gadget_rounding": float(0.5 * np.log2(v2)),
+                                       "fft_product": float(0.5 * np.log2(v3))},
+           "fft_product_error_log2_std": float(0.5 * np.log2(vprod)),
+           "variance_over_analytic": float(e.var() / (v1 + v2 + v3))}
+    if cpu_count > 0:
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle as O
+        ok = O.OracleKeys(O.default_params(), SEED)
+        allc, allm = np.concatenate(cts), np.concatenate(ms)
+        threads = os.cpu_count() or 1
+
+        def cpu_err(fn, cnt):
+            ref = fn(allc[:cnt], ok.test_vector(lut), threads=threads)
+            w = lut[allm[:cnt]].astype(np.uint64) * np.uint64(keys.params.delta())
+            return (ok.phase_big(ref) - w).view(np.int64).astype(np.float64)
+
+        e_fft = cpu_err(ok.pbs_fft, cpu_count)
+        res["vs_cpu_fft_restatement"] = {
+            "bootstraps": cpu_count, "cpu_log2_std": float(np.log2(e_fft.std())),
+            "variance_ratio_ci95": _ratio_ci(e[:cpu_count], e_fft)}
+        if exact_count > 0:
+            e_ex = cpu_err(ok.pbs_exact, exact_count)
+            res["vs_cpu_exact_restatement"] = {
+                "bootstraps": exact_count, "cpu_log2_std": float(np.log2(e_ex.std())),
+                "variance_ratio_ci95": _ratio_ci(e[:exact_count], e_ex),
+                "cpu_variance_over_analytic_without_fft_term": float(e_ex.var() / (v1 + v2))}
+    return res
 
 
 def program_cpu_baseline(plan, graph, per_level: int = 32):
@@ -400,11 +475,15 @@ def program_cpu_baseline(plan, graph, per_level: int = 32):
                       f"contraction of one sample ({1e3 * tc:.1f} ms)"}
 
 
-def graph_leg(args, pnb, world, rank, local, dist, dev, graph, B, seed, workload, metric,
-              cpu_baseline=None):
-    """Encrypted inference of `graph` over a B-sample shard per rank: device time of the
-    evaluation plus the output all-gather, and end to end with the host copies; rank 0 decrypts
-    the first samples of every rank and compares them with the cleartext graph."""
+def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, seed, workload,
+              metric, scaling, cpu_baseline=None):
+    """Encrypted inference of `graph` over `global_batch` samples sharded over the ranks
+    (contiguous shards, `pnb.shard`): each rank encrypts and evaluates its shard on its own GPU
+    (identical key replicas from one seed), one NCCL all-gather reassembles the output
+    ciphertexts on every rank.  `value` = global_batch / (max over ranks of the device time of
+    evaluation + all-gather); `e2e` adds this rank's host->device input copy and rank 0's
+    device->host copy of the gathered outputs.  Rank 0 decrypts EVERY sample and compares it
+    with the cleartext integer graph."""
     import numpy as np
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -412,16 +491,18 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, B, seed, workload
     plan = pnb.Plan(pnb.Graph(graph))
     ev = pnb.Evaluator(plan, device=local, seed=SEED)  # identical keys on every rank
     hi = (1 << graph["input_bits"]) - 1
-    rng = np.random.default_rng(seed + rank)
-    x = rng.integers(0, hi + 1, (B, plan.input_elems))
-    ct = ev.encrypt(x, seed=SEED + 7, first_index=rank * B * plan.input_elems)
-    ev.reserve(B)
+    x_all = np.random.default_rng(seed).integers(0, hi + 1, (global_batch, plan.input_elems))
+    a, b = pnb.shard(global_batch, world, rank)
+    B = b - a
+    # keystream indices follow the global sample index, so the ciphertexts of a sample are the
+    # same whatever the number of ranks
+    ct = ev.encrypt(x_all[a:b], seed=SEED + 7, first_index=a * plan.input_elems)
+    ev.reserve(max(B, 1))
     ev.evaluate(ct[:1])  # warm-up
     h_in = ct.cpu().pin_memory()
     d_in = torch.empty_like(ct)
-    gathered = torch.empty((world * B, plan.output_elems, ct.shape[-1]), dtype=torch.int64,
-                           device=dev)
-    h_out = torch.empty(gathered.shape, dtype=torch.int64).pin_memory()
+    h_out = torch.empty((global_batch, plan.output_elems, ct.shape[-1]),
+                        dtype=torch.int64).pin_memory()
     stream = torch.cuda.current_stream(dev)
     evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
     if dist is not None:
@@ -432,59 +513,69 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, B, seed, workload
     evs[1].record(stream)
     out = ev.evaluate(d_in)
     evs[2].record(stream)
-    if dist is not None:
-        gathered = pnb.gather_shards(out, world * B)  # rank r holds samples [r*B, (r+1)*B)
-    else:
-        gathered.copy_(out)
+    gathered = pnb.gather_shards(out, global_batch) if dist is not None else out
     evs[3].record(stream)
-    h_out.copy_(gathered, non_blocking=True)
+    if rank == 0:
+        h_out.copy_(gathered, non_blocking=True)
     evs[4].record(stream)
     torch.cuda.synchronize(dev)
     t_dev = evs[1].elapsed_time(evs[3])
     t_e2e = evs[0].elapsed_time(evs[4])
     t_gather = evs[2].elapsed_time(evs[3])
     if dist is not None:
-        t = torch.tensor([t_dev, t_e2e], dtype=torch.float64, device=dev)
+        t = torch.tensor([t_dev, t_e2e, t_gather], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_dev, t_e2e = float(t[0]), float(t[1])
-    ok = None
+        t_dev, t_e2e, t_gather = float(t[0]), float(t[1]), float(t[2])
+    checked, ok = 0, None
     if rank == 0:
         got = ev.decrypt(h_out.to(dev)).cpu().numpy()
         ok = True
-        for r in range(world):
-            xr = np.random.default_rng(seed + r).integers(0, hi + 1, (B, plan.input_elems))
-            for i in range(min(B, 2)):
-                want = ir_eval.evaluate(graph, {graph["inputs"][0]: xr[i].tolist()})
-                ok = ok and got[r * B + i].tolist() == want[graph["outputs"][0]]
+        for i in range(global_batch):
+            want = ir_eval.evaluate(graph, {graph["inputs"][0]: x_all[i].tolist()})
+            ok = ok and got[i].tolist() == want[graph["outputs"][0]]
+            checked += 1
     return {
-        "metric": metric, "value": world * B / (t_dev * 1e-3),
-        "unit": "samples/s", "samples_per_gpu": B, "global_batch": world * B,
-        "scaling": "weak", "ms": t_dev,
+        "metric": metric, "value": global_batch / (t_dev * 1e-3), "unit": "samples/s",
+        "global_batch": global_batch, "samples_per_gpu": B, "scaling": scaling, "ms": t_dev,
         "config": {"workload": workload,
                    "parallelism": f"samples sharded over {world} GPU(s), outputs all-gathered "
                                   "over NCCL"},
         "bootstraps_per_sample": plan.pbs_per_sample,
-        "bootstraps_by_key_set": [{"base_log": b, "levels": l, "per_sample": c}
-                                  for b, l, c in plan.key_sets()],
+        "bootstraps_by_key_set": [[bl, lv, c] for bl, lv, c in plan.key_sets()],
         "cpu_baseline": (cpu_baseline(plan, graph) if cpu_baseline is not None and rank == 0
                          and world == 1 and not args.no_cpu_baseline else None),
         "allgather_ms": t_gather,
-        "e2e": {"value": world * B / (t_e2e * 1e-3), "unit": "samples/s",
-                "h2d_bytes_per_step": int(h_in.numel() * 8),
-                "d2h_bytes_per_step": int(h_out.numel() * 8) if rank == 0 else 0},
-        "decrypt_ok": ok,
+        "e2e": {"value": global_batch / (t_e2e * 1e-3), "unit": "samples/s",
+                "h2d_bytes_per_step": int(global_batch * plan.input_elems * ct.shape[-1] * 8),
+                "d2h_bytes_per_step": int(h_out.numel() * 8)},
+        "decrypt_ok": ok, "samples_checked": checked,
     }
 
 
 def mlp_leg(args, pnb, world, rank, local, dist, dev):
-    """Encrypted MLP 784-128-128-10 (the reference quantizer's graph for that configuration)."""
+    """Encrypted MLP 784-128-128-10 (the reference quantizer's graph for that configuration) on
+    a fixed global batch sharded over the ranks (strong scaling)."""
     with open(os.path.join(ROOT, "tests", "golden", "cfg4_mlp.json")) as f:
         graph = json.load(f)["graph"]
     return graph_leg(args, pnb, world, rank, local, dist, dev, graph, args.mlp_batch,
                      SEED + 100,
                      "MLP 784-128-128-10, ReLU fused in Requant, PTQ n_bits=6 (reference "
                      "quantizer graph), 6-bit inputs",
-                     "encrypted_mlp_samples_per_second", cpu_baseline=program_cpu_baseline)
+                     "encrypted_mlp_samples_per_second", "strong",
+                     cpu_baseline=program_cpu_baseline)
+
+
+def cnn_leg(args, pnb, world, rank, local, dist, dev):
+    """Encrypted small CNN (Conv 3x3x8 s1 -> ReLU -> avg pool 2x2 -> Conv 3x3x16 s2 -> ReLU ->
+    Linear 576->10; the reference quantizer's graph) on `--cnn-batch` samples per GPU (weak
+    scaling: 8 GPUs evaluate the configuration's 512-sample batch)."""
+    with open(os.path.join(ROOT, "tests", "golden", "cfg5_cnn.json")) as f:
+        graph = json.load(f)["graph"]
+    return graph_leg(args, pnb, world, rank, local, dist, dev, graph, args.cnn_batch * world,
+                     SEED + 300,
+                     "CNN 1x28x28: Conv 3x3x8 s1, ReLU, avg pool 2x2, Conv 3x3x16 s2, ReLU, "
+                     "Linear 576->10 (reference quantizer graph, n_bits=6), 6-bit inputs",
+                     "encrypted_cnn_samples_per_second", "weak")
 
 
 def linear_requant_graph():
@@ -505,10 +596,10 @@ def linear_requant_graph():
 def linear_requant_leg(args, pnb, world, rank, local, dist, dev):
     """The Linear 784 -> 128 + Requant configuration end to end (contraction + bootstraps)."""
     return graph_leg(args, pnb, world, rank, local, dist, dev, linear_requant_graph(),
-                     args.lr_batch, SEED + 200,
+                     args.lr_batch * world, SEED + 200,
                      "Linear 784->128 (int4 weights U[-8,7]) + ReLU-Requant to 2 bits, 6-bit "
                      "inputs, N=2048 parameter set",
-                     "encrypted_linear_requant_samples_per_second",
+                     "encrypted_linear_requant_samples_per_second", "weak",
                      cpu_baseline=program_cpu_baseline)
 
 
@@ -551,23 +642,35 @@ def run_gpu(args):
     dec = pnb.decrypt_vec(keys, out).cpu().numpy()
     decrypt_ok = bool(np.array_equal(dec, lut[msgs]))
 
+    # With N > 1 ranks each step is one sharded layer of bootstraps: every rank bootstraps its
+    # own 4096 ciphertexts, then one NCCL all-gather reassembles the layer's outputs on every
+    # rank (the exchange step of the sample-sharded evaluation).
+    gathered = (torch.empty((world * B, keys.big_dim + 1), dtype=torch.int64, device=dev)
+                if dist is not None else None)
+    if dist is not None:
+        dist.all_gather_into_tensor(gathered, out)  # warm the communicator
+
     # timed region: K steps, L2 flushed between steps (outside the step events)
-    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
-           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4))
+          for _ in range(args.steps)]
     barrier()
     with ClockSampler(local) as clk:
         for i in range(args.steps):
             flush.zero_()
-            e0, e1, e2 = ev[i]
+            e0, e1, e2, e3 = ev[i]
             e0.record(stream)
             pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
             e1.record(stream)
             pnb.blind_rotate(keys, tv, small, out=out)
             e2.record(stream)
+            if dist is not None:
+                dist.all_gather_into_tensor(gathered, out)
+            e3.record(stream)
         barrier()
-    step_ms = [a.elapsed_time(c) for a, b, c in ev]
-    br_ms = [b.elapsed_time(c) for a, b, c in ev]
-    ks_ms = [a.elapsed_time(b) for a, b, c in ev]
+    step_ms = [a.elapsed_time(d) for a, b, c, d in ev]
+    br_ms = [b.elapsed_time(c) for a, b, c, d in ev]
+    ks_ms = [a.elapsed_time(b) for a, b, c, d in ev]
+    ag_ms = [c.elapsed_time(d) for a, b, c, d in ev]
     total_ms = sum(step_ms)
     if dist is not None:
         t = torch.tensor([total_ms], dtype=torch.float64, device=dev)
@@ -635,48 +738,54 @@ def run_gpu(args):
                 "kernel": "blind_rotate_kernel<4>",
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
-    mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
-    lin_rq = (None if args.lr_batch <= 0
-              else linear_requant_leg(args, pnb, world, rank, local, dist, dev))
     contraction = None if args.contract_batch <= 0 else contraction_leg(args, pnb, local, dev,
                                                                            flush)
-    noise = noise_leg(pnb, keys, dev) if (rank == 0 and args.noise) else None
+    noise = (noise_leg(pnb, keys, dev, args.noise_cpu if world == 1 else 0,
+                       args.noise_exact if world == 1 else 0)
+             if (rank == 0 and args.noise) else None)
     sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
     key_sets = key_set_leg(pnb, dev, flush) if (rank == 0 and args.key_sets) else None
+    lin_rq = (None if args.lr_batch <= 0
+              else linear_requant_leg(args, pnb, world, rank, local, dist, dev))
+    cnn = None if args.cnn_batch <= 0 else cnn_leg(args, pnb, world, rank, local, dist, dev)
+    mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         v, info = cpu_reference_run(args, args.ref_samples, 1, args.ref_steps)
         cpu = {"value": v, "unit": "PBS/s", "cores": info["threads"], "kind": "port",
                "sample": f"{args.ref_samples} PBS x {args.ref_steps} passes of the same "
-                         f"workload (oracle f64-FFT PBS, {info['threads']} host threads)"}
+                         f"workload (the oracle's unvectorised f64-FFT PBS restatement, "
+                         f"{info['threads']} host threads)"}
 
     if dist is not None:
         dist.barrier()
     if rank == 0:
         clocks = clk.summary()
+        # the large per-leg objects go last, in increasing order of importance, so that a
+        # reader that keeps only the end of the line keeps the configuration legs
         line = {
             "metric": "pbs_per_second", "value": value, "unit": "PBS/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": total_ms / args.steps, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "batch_per_gpu": B, "global_batch": B * world,
-                       "parallelism": f"replicas{world}",
-                       "l2": "flushed (256 MB write) between timed steps"},
+            "config": pbs_config(B, world),
             "e2e": {"value": e2e_value, "unit": "PBS/s",
                     "h2d_bytes_per_step": int(h_in.numel() * 8),
                     "d2h_bytes_per_step": int(h_out.numel() * 8),
                     "pipelining": "upload and download streams, two device buffers"},
             "roofline": roofline, "cpu_baseline": cpu, "clocks": clocks,
             "gpu_launches": 3 * args.steps,
-            "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg},
+            "stage_ms": {"keyswitch": sum(ks_ms) / len(ks_ms), "blind_rotate": br_avg,
+                         "allgather": sum(ag_ms) / len(ag_ms)},
             "decrypt_ok": decrypt_ok and e2e_ok,
-            "mlp": mlp,
-            "linear_requant": lin_rq,
-            "contraction": contraction,
-            "noise": noise,
             "pbs_batch_sweep": sweep,
             "pbs_by_key_set": key_sets,
+            "noise": noise,
+            "contraction": contraction,
+            "linear_requant": lin_rq,
+            "cnn": cnn,
+            "mlp": mlp,
         }
         print(json.dumps(line), flush=True)
     if dist is not None:
@@ -733,10 +842,19 @@ def main():
                     help="PBS/s of the multi-level key sets at batch 4096 (rank 0)")
     ap.add_argument("--noise", type=int, default=1,
                     help="measure the bootstrap output noise over ~1e5 bootstraps (rank 0)")
-    ap.add_argument("--lr-batch", type=int, default=64,
+    ap.add_argument("--lr-batch", type=int, default=32,
                     help="samples per GPU of the Linear 784->128 + Requant leg (0 skips it)")
-    ap.add_argument("--mlp-batch", type=int, default=32,
-                    help="encrypted MLP samples per GPU (0 skips the MLP leg)")
+    ap.add_argument("--mlp-batch", type=int, default=1024,
+                    help="global batch of the encrypted MLP leg, sharded over the GPUs "
+                         "(strong scaling; 0 skips it)")
+    ap.add_argument("--cnn-batch", type=int, default=64,
+                    help="encrypted CNN samples per GPU (weak scaling; 0 skips the CNN leg)")
+    ap.add_argument("--noise-cpu", type=int, default=8192,
+                    help="bootstraps the f64-FFT CPU restatement repeats for the noise "
+                         "comparison (one GPU only)")
+    ap.add_argument("--noise-exact", type=int, default=512,
+                    help="bootstraps the exact-arithmetic CPU restatement repeats for the noise "
+                         "comparison (one GPU only)")
     args = ap.parse_args()
     if args.summarize_launches:
         summarize_launches(args.summarize_launches)

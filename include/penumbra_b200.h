@@ -10,7 +10,10 @@
  *   - ciphertexts are u64 words mod 2^64: an LWE ciphertext of dimension d is d+1 words with
  *     the body last; batches are contiguous [count][d+1];
  *   - `stream` is a cudaStream_t (NULL = legacy default stream); calls are asynchronous on it
- *     unless documented otherwise and are thread-compatible (one stream per caller thread).
+ *     unless documented otherwise and are thread-compatible (one stream per caller thread);
+ *   - key sets and the per-device FFT tables the library builds at the first key set on a
+ *     device live in that device's primary context: a cudaDeviceReset invalidates them, and
+ *     the library must not be used on that device again in the same process.
  */
 #ifndef PENUMBRA_B200_H
 #define PENUMBRA_B200_H
@@ -132,11 +135,11 @@ int pnb_pbs_batch(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* 
  * that must not pay allocator latency or synchronisation, FFI callers that keep a fixed device
  * footprint after start-up).  The scratch is a fixed 4 MiB array that every GPU loading the
  * library holds until exit; with the default parameter set a call takes at most 247
- * ciphertexts and larger counts are rejected with PNB_ERR_INVALID (split the batch).  The
- * first call on a device looks up that array's device address; make that first call before
- * any stream capture.  Calls share the array: calls that overlap on the GPU race and must be
- * serialised by the caller.  The key set must come from pnb_keygen or pnb_keys_import on the
- * same device.
+ * ciphertexts and larger counts are rejected with PNB_ERR_INVALID (split the batch).  Every
+ * call looks up that array's device address on the current device (a lookup that allocates
+ * nothing); make the first call on a device before any stream capture.  Calls share the array:
+ * calls that overlap on the GPU race and must be serialised by the caller.  The key set must
+ * come from pnb_keygen or pnb_keys_import on the same device.
  * No counterpart in the reference. */
 int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const uint64_t* in_dev,
                           uint64_t* out_dev, int count, void* stream);
@@ -146,9 +149,14 @@ int pnb_pbs_batch_noalloc(const pnb_keys* keys, const uint64_t* tv_dev, const ui
  * (msg_bits bits plus carries, delta 2^(63 - msg_bits - carry_bits)), as the reference encrypts
  * a signed radix integer.  out_dev [count][k*N+1] receives each integer v as v * delta_out
  * (mod 2^64).  With is_signed the top block's digit is read as two's complement and carries
- * above it are dropped.  Costs one bootstrap per block plus one sum.  The noise is the sum of
- * num_blocks bootstrap outputs, so decryption needs delta_out well above that noise and
- * |v| * delta_out < 2^62.  Requires num_blocks * msg_bits <= 63.
+ * above it are dropped; the result equals decrypt_signed's whenever the lower blocks' weighted
+ * sum stays below the top block's weight, which holds for carry-free lower blocks (as
+ * encrypt_signed and every carry-propagating radix op leave them).  Costs one bootstrap per
+ * block plus one sum, with `keys`' gadget: the noise is the sum of num_blocks bootstrap
+ * outputs of that key set, so decryption needs delta_out well above it (a multi-level key set
+ * from the same seed merges wider integers) and |v| * delta_out < 2^62.  Requires
+ * num_blocks * msg_bits <= 63 and num_blocks * 2^(msg_bits + carry_bits) <= 1024.  Allocates
+ * its scratch from the stream-ordered allocator and does not synchronise the stream.
  * Replaces: RadixClientKey::encrypt_signed / decrypt_signed's block encoding at a graph
  * boundary (runtime/src/encrypt.rs:20-22, 43-45): ciphertexts in the reference's radix form
  * enter the wide-ciphertext kernels. */

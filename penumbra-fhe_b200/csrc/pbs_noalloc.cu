@@ -13,8 +13,6 @@
 // writes every scratch word it reads, so nothing needs clearing.  Calls whose kernels overlap on
 // the GPU (different streams, or different host threads) race on the array and must be
 // serialised by the caller.
-#include <mutex>
-
 #include "pnb_internal.cuh"
 #include "pnb_keys.h"
 
@@ -23,24 +21,15 @@ namespace pnb {
 constexpr size_t NOALLOC_SCRATCH_BYTES = 4u << 20;  // 4 MiB
 static __device__ __align__(256) unsigned char g_pbs_scratch[NOALLOC_SCRATCH_BYTES];
 
-// Device address of g_pbs_scratch for each device (host code must not use the symbol itself:
-// in host code it is only a stand-in for the device object).
-static std::mutex g_noalloc_mu;
-static void* g_noalloc_ptr[64];
-
-static int noalloc_scratch(int dev, void** out) {
-  if (dev < 0 || dev >= 64) {
-    set_error("pbs_noalloc: device index %d out of range", dev);
-    return PNB_ERR_INVALID;
-  }
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&p, g_pbs_scratch);  // `dev` is current here
-    if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(pbs scratch)");
-    g_noalloc_ptr[dev] = p;
-  }
-  *out = g_noalloc_ptr[dev];
+// Device address of g_pbs_scratch on the current device.  Host code must not hand the symbol
+// itself to a kernel: in host code it is only a stand-in for the device object.  The address is
+// looked up on every call (the lookup allocates nothing), so a caller that resets the device or
+// replaces its context never reaches a stale pointer.
+static int noalloc_scratch(void** out) {
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, g_pbs_scratch);
+  if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(pbs scratch)");
+  *out = p;
   return PNB_OK;
 }
 
@@ -60,10 +49,8 @@ int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in,
               "with pnb_keygen or pnb_keys_import on this device first");
     return PNB_ERR_INVALID;
   }
-  int dev = 0;
-  PNB_CUDA(cudaGetDevice(&dev));
   void* scratch = nullptr;
-  int rc = noalloc_scratch(dev, &scratch);
+  int rc = noalloc_scratch(&scratch);
   if (rc) return rc;
   return pbs_batch(K, tv, in, out, count, scratch, NOALLOC_SCRATCH_BYTES, st);
 }

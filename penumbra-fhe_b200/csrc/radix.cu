@@ -12,7 +12,6 @@
 // by the block weight.
 #include <algorithm>
 #include <climits>
-#include <vector>
 
 #include "pnb_internal.cuh"
 #include "pnb_keys.h"
@@ -39,7 +38,34 @@ __global__ void radix_iota_kernel(int32_t* idx, int n) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) idx[i] = i;
 }
 
+// Lookup tables of every block, passed by value so that building the test vectors needs no
+// host-to-device copy (a copy from pageable host memory would synchronise the stream).
+constexpr int RADIX_LUT_WORDS = 1024;
+struct RadixLuts {
+  uint64_t v[RADIX_LUT_WORDS];  // [block][lut_len]
+};
+
+// Test vector of block blockIdx.y: box m of width N / lut_len holds lut[m] * delta_out, rotated
+// by half a box, negated past the half torus (the encoding pnb_test_vector builds).
+__global__ void radix_tv_kernel(const RadixLuts luts, int lut_len, uint64_t delta_out, int N,
+                                uint64_t* __restrict__ tvs) {
+  const int i = blockIdx.y;
+  const uint64_t* lut = luts.v + i * lut_len;
+  const int box = N / lut_len, half = box / 2;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < N; j += gridDim.x * blockDim.x) {
+    const int m = (j + half) / box;
+    tvs[(size_t)i * N + j] =
+        (m < lut_len) ? lut[m] * delta_out : (uint64_t)0 - lut[m - lut_len] * delta_out;
+  }
+}
+
 // Lookup table of block `i` of `nb`: entry d (digit plus carries) -> its weighted value.
+// Unsigned integers and the lower blocks of signed ones keep their carries (d * 2^(mb i)).
+// The top block of a signed integer reads its digit as two's complement and drops the carries
+// above it, which lie beyond the integer's width.  The merged value then equals
+// decrypt_signed's (the blocks' sum reduced to the integer's width and sign-extended) whenever
+// the lower blocks' weighted sum stays below the top block's weight -- always for carry-free
+// lower blocks, which is how encrypt_signed and every carry-propagating radix op leave them.
 void radix_merge_lut(int msg_bits, int carry_bits, int nb, int i, bool is_signed,
                      uint64_t* lut) {
   const int len = 1 << (msg_bits + carry_bits);
@@ -47,8 +73,6 @@ void radix_merge_lut(int msg_bits, int carry_bits, int nb, int i, bool is_signed
   const uint64_t weight = (uint64_t)1 << (msg_bits * i);
   for (int d = 0; d < len; ++d) {
     if (is_signed && i == nb - 1) {
-      // carries above the top digit lie beyond the integer's width: dropped, as the
-      // two's-complement decryption drops them
       const int64_t dm = d % mod;
       const int64_t sd = dm >= mod / 2 ? dm - mod : dm;
       lut[d] = (uint64_t)sd * weight;
@@ -69,9 +93,14 @@ int radix_merge(const pnb_keys* K, const uint64_t* blocks, int nb, int count, bo
     set_error("radix_merge: %d integers x %d blocks exceed one launch", count, nb);
     return PNB_ERR_INVALID;
   }
+  const int lut_len = 1 << (mb + cb);
+  if ((long long)nb * lut_len > RADIX_LUT_WORDS || lut_len > K->p.N) {
+    set_error("radix_merge: %d blocks of %d-entry tables exceed the %d table words a call takes",
+              nb, lut_len, RADIX_LUT_WORDS);
+    return PNB_ERR_INVALID;
+  }
   if (count == 0) return PNB_OK;
   const int N = K->p.N, L = K->p.k * N + 1, total = count * nb;
-  const int lut_len = 1 << (mb + cb);
   const size_t tv_b = radix_align256((size_t)nb * N * sizeof(uint64_t));
   const size_t idx_b = radix_align256((size_t)nb * sizeof(int32_t));
   const size_t small_b = radix_align256((size_t)total * (K->p.n + 1) * sizeof(uint64_t));
@@ -86,10 +115,13 @@ int radix_merge(const pnb_keys* K, const uint64_t* blocks, int nb, int count, bo
   void* digits = w + tv_b + idx_b + small_b + parts_b;
 
   int rc = PNB_OK;
-  std::vector<uint64_t> lut(lut_len);
-  for (int i = 0; i < nb && rc == PNB_OK; ++i) {
-    radix_merge_lut(mb, cb, nb, i, is_signed, lut.data());
-    rc = test_vector(K, lut.data(), lut_len, delta_out, tvs + (size_t)i * N, st);
+  {
+    RadixLuts luts{};
+    for (int i = 0; i < nb; ++i)
+      radix_merge_lut(mb, cb, nb, i, is_signed, luts.v + (size_t)i * lut_len);
+    radix_tv_kernel<<<dim3((N + 255) / 256, nb), 256, 0, st>>>(luts, lut_len, delta_out, N, tvs);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) rc = cuda_status(e, "radix_tv_kernel");
   }
   if (rc == PNB_OK) {
     radix_iota_kernel<<<1, 64, 0, st>>>(idx, nb);

@@ -73,3 +73,42 @@ def test_merge_rejects_bad_shapes(pnb, rkeys):
     with pytest.raises(pnb.LibraryError, match="63-bit"):
         pnb.radix_merge(rkeys, torch.zeros((1, 32, L), dtype=torch.int64, device="cuda:0"),
                         1 << 56)
+
+
+def test_merge_signed_lower_carries_within_width(pnb, rkeys):
+    # lower blocks that still hold carries: the merge equals decrypt_signed's reading (the
+    # blocks' sum reduced to the 6-bit width, sign-extended) while the lower blocks' weighted
+    # sum stays below the top block's weight (16)
+    digits = np.array([[5, 1, 1], [7, 2, 3], [13, 0, 2], [4, 2, 2], [9, 1, 0]])
+    width = 6
+
+    def decrypt_signed(d):
+        u = sum(int(x) << (2 * i) for i, x in enumerate(d)) % (1 << width)
+        return u - (1 << width) if u >= 1 << (width - 1) else u
+
+    want = np.array([decrypt_signed(d) for d in digits])
+    blocks = _encrypt_blocks(pnb, rkeys, digits, SEED + 5)
+    out = pnb.radix_merge(rkeys, blocks, 1 << 56, signed=True)
+    got, _ = _decode(pnb, rkeys, out, 56)
+    assert np.array_equal(got, want)
+
+
+def test_merge_22bit_integers_with_a_multilevel_key_set(pnb):
+    # The merged noise is the sum of one bootstrap output per block: 11 blocks through the
+    # (2^7, 6) key set (output noise 2^33.8 each) decrypt exactly at delta 2^39, where the
+    # single-level set (2^49 each) is limited to about 8-bit integers.
+    p = pnb.default_params()
+    p.pbs_base_log, p.pbs_level = 7, 6
+    keys = pnb.keygen(p, seed=SEED, device=0)
+    rng = np.random.default_rng(SEED + 6)
+    nb, count = 11, 512
+    v = rng.integers(-(1 << 21), 1 << 21, count)
+    v[:4] = [-(1 << 21), (1 << 21) - 1, 0, -1]
+    u = v & ((1 << (2 * nb)) - 1)
+    digits = np.stack([(u >> (2 * i)) & 3 for i in range(nb)], axis=1)
+    blocks = _encrypt_blocks(pnb, keys, digits, SEED + 7)
+    out = pnb.radix_merge(keys, blocks, 1 << 39, signed=True)
+    got, err = _decode(pnb, keys, out, 39)
+    assert np.array_equal(got, v)
+    assert np.log2(err.astype(np.float64).std()) < 36.5
+    assert pnb.device_status(0) == 0
