@@ -284,6 +284,84 @@ int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys);
 int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t* out_dev,
                  void* stream);
 
+/* ---- One op at a time --------------------------------------------------------------------
+ * The same exact programs, compiled for a single IR op whose inputs arrive from earlier ops, so
+ * that an FFI shell keeping the reference's node walk (runtime/src/eval.rs:104-153) can route
+ * each node to the GPU: Linear / Conv2d / avg Pool to pnb_lwe_contract(_gather), everything
+ * else to a one-op plan run on a key ring.  A tensor is described by pnb_tensor_desc; the
+ * output descriptor of one op is the input descriptor of the next. */
+typedef struct pnb_keyring pnb_keyring;
+
+typedef struct pnb_tensor_desc {
+  int64_t elems;      /* elements (ciphertexts) per sample */
+  int64_t lo, hi;     /* every element's integer value lies in [lo, hi] */
+  int32_t scale_log2; /* each element encrypts v * 2^scale_log2 (0 in an input: planner's choice) */
+  int32_t reserved;
+  double log2_sigma;  /* noise std of the elements, log2 of torus units (0: a fresh encryption) */
+} pnb_tensor_desc;
+
+/* Every key set the exact programs may bootstrap with (the planner's gadget menu for `params`),
+ * generated on `device` from one seed: all share the secret keys and the keyswitching key, so
+ * ciphertexts pass between them freely.  Blocking.
+ * Replaces: keys::keygen + the ServerKey an EvalCtx borrows (runtime/src/keys.rs:47-56,
+ * runtime/src/ops/mod.rs:64-69). */
+int pnb_keyring_create(int device, const pnb_params* params, uint64_t seed, pnb_keyring** out);
+int pnb_keyring_free(pnb_keyring* ring);
+/* Key set `idx` of the ring (borrowed); set 0 is the client's: encrypt and decrypt with it. */
+int pnb_keyring_keys(const pnb_keyring* ring, int idx, pnb_keys** keys);
+
+/* Compile one IR op (its JSON payload, as in a node's "op") over n_inputs (1, or 2 for Add)
+ * input tensors described by `in`; out_scale_log2 (0: the planner's choice) pins the output's
+ * scale and out_log2_sigma (0: decryptable with the margin) bounds the output's noise, so that
+ * the ops after it can read it exactly.  Fails with the reference's validation message, or when no exact program exists for
+ * the inputs' noise and range.  The plan's input/output tensors are read back with
+ * pnb_plan_tensor_desc.  Replaces: OpSpec::build + Op::eval for one node
+ * (runtime/src/ir.rs:197-452, runtime/src/ops/mod.rs:77-138). */
+int pnb_op_plan_create(const char* op_json, size_t len, const pnb_params* params,
+                       const pnb_tensor_desc* in, int n_inputs, int out_scale_log2,
+                       double out_log2_sigma, double margin_sigmas, pnb_plan** out);
+int pnb_plan_tensor_desc(const pnb_plan* plan, int is_output, int idx, pnb_tensor_desc* desc);
+/* An evaluator of `plan` that borrows the ring's key sets (no key generation) on the ring's
+ * device.  The ring must outlive the evaluator. */
+int pnb_evaluator_create_with(const pnb_plan* plan, const pnb_keyring* ring, size_t max_bytes,
+                              pnb_evaluator** out);
+
+/* Requant parameters: per-tensor (channels = 1) or per-channel (element e uses channel
+ * e / channel_size), as the IR's Requant op carries them. */
+typedef struct pnb_requant_spec {
+  int32_t channels;
+  int32_t out_bits;            /* <= 2 (MESSAGE_BITS) */
+  int64_t channel_size;
+  const uint64_t* mult;        /* [channels], each >= 1 */
+  const uint64_t* round_bias;  /* [channels] */
+  const uint32_t* shift;       /* [channels] */
+  const uint64_t* clamp_lut;   /* [2^out_bits]; NULL = identity */
+} pnb_requant_spec;
+
+/* clamp_lut[min((max(v,0) * mult + round_bias) >> shift, 2^out_bits - 1)] of every element of
+ * `batch` samples: in_dev [batch][in->elems][kN+1] wide ciphertexts, out_dev
+ * [batch][in->elems][kN+1] at scale out_scale_log2 with noise below out_log2_sigma (0: the
+ * planner's choice, as in pnb_op_plan_create; *out_desc, if given, receives the output's
+ * descriptor).  Exact: decrypted outputs equal the integer op.
+ * Blocking (compiles the element-wise program, runs it, synchronises `stream`).
+ * Replaces: Requant::eval (runtime/src/ops/requant.rs:126-241). */
+int pnb_requant_batch(const pnb_keyring* ring, const pnb_requant_spec* spec,
+                      const pnb_tensor_desc* in, const uint64_t* in_dev, int batch,
+                      int out_scale_log2, double out_log2_sigma, uint64_t* out_dev,
+                      pnb_tensor_desc* out_desc, void* stream);
+/* [v >= threshold] of a single-element tensor per sample (out_dev [batch][1][kN+1]).
+ * Blocking.  Replaces: Argmax::eval (runtime/src/ops/argmax.rs:22-35). */
+int pnb_argmax_batch(const pnb_keyring* ring, int64_t threshold, const pnb_tensor_desc* in,
+                     const uint64_t* in_dev, int batch, int out_scale_log2,
+                     double out_log2_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc,
+                     void* stream);
+/* a + b element-wise (both tensors at the same scale; out_scale_log2 0 or that scale).
+ * Blocking.  Replaces: Add::eval_n (runtime/src/ops/add.rs:37-58). */
+int pnb_add_batch(const pnb_keyring* ring, const pnb_tensor_desc* a, const uint64_t* a_dev,
+                  const pnb_tensor_desc* b, const uint64_t* b_dev, int batch, int out_scale_log2,
+                  double out_log2_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc,
+                  void* stream);
+
 #ifdef __cplusplus
 }
 #endif

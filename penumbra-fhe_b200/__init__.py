@@ -22,6 +22,7 @@ __all__ = [
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
     "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys", "radix_merge",
+    "TensorDesc", "KeyRing", "op_plan", "requant_batch", "argmax_batch", "add_batch",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -118,6 +119,23 @@ _SIGS = {
     "pnb_evaluator_keys": (C.c_int, [C.c_void_p, C.POINTER(C.c_void_p)]),
     "pnb_evaluator_reserve": (C.c_int, [C.c_void_p, C.c_int]),
     "pnb_evaluate": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p]),
+    "pnb_keyring_create": (C.c_int, [C.c_int, C.POINTER(Params), C.c_uint64,
+                                     C.POINTER(C.c_void_p)]),
+    "pnb_keyring_free": (C.c_int, [C.c_void_p]),
+    "pnb_keyring_keys": (C.c_int, [C.c_void_p, C.c_int, C.POINTER(C.c_void_p)]),
+    "pnb_op_plan_create": (C.c_int, [C.c_char_p, C.c_size_t, C.POINTER(Params), C.c_void_p,
+                                     C.c_int, C.c_int, C.c_double, C.c_double,
+                                     C.POINTER(C.c_void_p)]),
+    "pnb_plan_tensor_desc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "pnb_evaluator_create_with": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t,
+                                            C.POINTER(C.c_void_p)]),
+    "pnb_requant_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                    C.c_int, C.c_double, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "pnb_argmax_batch": (C.c_int, [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int,
+                                   C.c_int, C.c_double, C.c_void_p, C.c_void_p, C.c_void_p]),
+    "pnb_add_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                C.c_int, C.c_int, C.c_double, C.c_void_p, C.c_void_p,
+                                C.c_void_p]),
 }
 
 _LIB = None
@@ -561,6 +579,25 @@ class Plan:
         self.inputs = [self._tensor(0, i) for i in range(s.num_inputs)]
         self.outputs = [self._tensor(1, i) for i in range(s.num_outputs)]
 
+    def _init_from_handle(self, h, params: Params):
+        self.params = params
+        self._h = h
+        s = _PlanSummary()
+        _check("pnb_plan_info", lib().pnb_plan_info(h, C.byref(s)))
+        self.input_elems = s.input_elems
+        self.output_elems = s.output_elems
+        self.pbs_per_sample = s.pbs_per_sample
+        self.cost_per_sample = s.cost_per_sample
+        self.num_instructions = s.num_instructions
+        self.inputs = [self._tensor(0, i) for i in range(s.num_inputs)]
+        self.outputs = [self._tensor(1, i) for i in range(s.num_outputs)]
+
+    def desc(self, is_output: bool, idx: int = 0) -> "TensorDesc":
+        d = TensorDesc()
+        _check("pnb_plan_tensor_desc",
+               lib().pnb_plan_tensor_desc(self._h, int(is_output), idx, C.byref(d)))
+        return d
+
     def _tensor(self, is_out, i):
         e, sc, lo, hi = C.c_int64(), C.c_int(), C.c_int64(), C.c_int64()
         _check("pnb_plan_tensor", lib().pnb_plan_tensor(self._h, is_out, i, C.byref(e),
@@ -603,16 +640,22 @@ class Plan:
 class Evaluator:
     """A plan bound to one GPU with its key sets (``EvalCtx`` + ``evaluate_graph``)."""
 
-    def __init__(self, plan: Plan, device: int = 0, seed: int = 0, max_bytes: int = 0):
+    def __init__(self, plan: Plan, device: int = 0, seed: int = 0, max_bytes: int = 0,
+                 ring: "KeyRing | None" = None):
         self.plan = plan
-        self.device = device
+        self.device = device if ring is None else ring.device
+        self._ring = ring  # a borrowing evaluator keeps its ring alive
         h = C.c_void_p()
-        _check("pnb_evaluator_create",
-               lib().pnb_evaluator_create(plan._h, device, seed, max_bytes, C.byref(h)))
+        if ring is None:
+            _check("pnb_evaluator_create",
+                   lib().pnb_evaluator_create(plan._h, device, seed, max_bytes, C.byref(h)))
+        else:
+            _check("pnb_evaluator_create_with",
+                   lib().pnb_evaluator_create_with(plan._h, ring._h, max_bytes, C.byref(h)))
         self._h = h
         k = C.c_void_p()
         _check("pnb_evaluator_keys", lib().pnb_evaluator_keys(h, C.byref(k)))
-        self.keys = KeySet(k, plan.params, device, seed, owner=self)
+        self.keys = KeySet(k, plan.params, self.device, seed, owner=self)
         self.row = plan.params.k * plan.params.N + 1
 
     def reserve(self, batch: int):
@@ -704,3 +747,130 @@ def evaluate_sharded(ev: "Evaluator", ct_all: torch.Tensor, group=None) -> torch
     local = ev.evaluate(ct_all[a:b].contiguous()) if b > a else torch.empty(
         (0, ev.plan.output_elems, ev.row), dtype=torch.int64, device=ct_all.device)
     return gather_shards(local, ct_all.shape[0], group)
+
+
+# ---- one op at a time ----------------------------------------------------------------------
+
+class TensorDesc(C.Structure):
+    """``pnb_tensor_desc``: elements per sample, value range, plaintext scale, noise."""
+    _fields_ = [("elems", C.c_int64), ("lo", C.c_int64), ("hi", C.c_int64),
+                ("scale_log2", C.c_int32), ("reserved", C.c_int32), ("log2_sigma", C.c_double)]
+
+    @classmethod
+    def make(cls, elems: int, lo: int, hi: int, scale_log2: int = 0, log2_sigma: float = 0.0):
+        return cls(elems, lo, hi, scale_log2, 0, log2_sigma)
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_ if f != "reserved"}
+
+
+class KeyRing:
+    """Every key set the exact op programs may bootstrap with, from one seed on one GPU
+    (``pnb_keyring``); ``keys`` is the client set that encrypts and decrypts."""
+
+    def __init__(self, params: Params | None = None, seed: int = 0, device: int = 0):
+        self.params = default_params() if params is None else params
+        self.device = device
+        h = C.c_void_p()
+        _check("pnb_keyring_create",
+               lib().pnb_keyring_create(device, C.byref(self.params), seed, C.byref(h)))
+        self._h = h
+        k = C.c_void_p()
+        _check("pnb_keyring_keys", lib().pnb_keyring_keys(h, 0, C.byref(k)))
+        self.keys = KeySet(k, self.params, device, seed, owner=self)
+        self.row = self.params.k * self.params.N + 1
+
+    def encrypt(self, values, scale_log2: int, seed: int, first_index: int = 0) -> torch.Tensor:
+        """Encrypt integers (any shape [batch, elems]) at 2^scale_log2."""
+        v = torch.as_tensor(values, dtype=torch.int64)
+        ct = encrypt(self.keys, v.reshape(-1), seed, first_index, delta=1 << scale_log2)
+        return ct.reshape(tuple(v.shape) + (self.row,))
+
+    def decrypt(self, ct: torch.Tensor, scale_log2: int) -> torch.Tensor:
+        """Signed rounding of every ciphertext's phase at 2^scale_log2."""
+        ph = phase(self.keys, ct.reshape(-1, self.row)).reshape(ct.shape[:-1])
+        return torch.bitwise_right_shift(ph + (1 << (scale_log2 - 1)), scale_log2)
+
+    def __del__(self):
+        try:
+            if self._h:
+                lib().pnb_keyring_free(self._h)
+                self._h = None
+        except Exception:
+            pass
+
+
+def op_plan(op: dict, inputs: list[TensorDesc], params: Params | None = None,
+            out_scale: int = 0, out_sigma: float = 0.0, margin_sigmas: float = 0.0) -> Plan:
+    """Compile one IR op over described inputs (``pnb_op_plan_create``) into a ``Plan``."""
+    import json as _json
+    params = default_params() if params is None else params
+    text = _json.dumps(op).encode()
+    arr = (TensorDesc * len(inputs))(*inputs)
+    h = C.c_void_p()
+    _check("pnb_op_plan_create",
+           lib().pnb_op_plan_create(text, len(text), C.byref(params), C.cast(arr, C.c_void_p),
+                                    len(inputs), out_scale, out_sigma, margin_sigmas,
+                                    C.byref(h)))
+    pl = Plan.__new__(Plan)
+    pl._init_from_handle(h, params)
+    return pl
+
+
+def _op_call(fn: str, ring: KeyRing, args_before, descs, tensors, out_elems: int,
+             out_scale: int, out_sigma: float, out: torch.Tensor | None):
+    batch = tensors[0].shape[0]
+    dev = tensors[0].device
+    if out is None:
+        out = torch.empty((batch, out_elems, ring.row), dtype=torch.int64, device=dev)
+    od = TensorDesc()
+    ptrs = []
+    for d, t in zip(descs, tensors):
+        if t.shape[1] != d.elems or t.shape[2] != ring.row:
+            raise ValueError(f"tensor of shape {tuple(t.shape)} does not match its descriptor "
+                             f"({d.elems} elements of {ring.row} words)")
+        ptrs += [C.byref(d), _ptr(_u64(t).contiguous())]
+    _check(fn, getattr(lib(), fn)(ring._h, *args_before, *ptrs, batch, out_scale,
+                                  C.c_double(out_sigma), _ptr(out), C.byref(od), _stream(dev)))
+    return out, od
+
+
+def requant_batch(ring: KeyRing, x: torch.Tensor, desc: TensorDesc, shift, mult=1,
+                  round_bias=0, out_bits: int = 2, clamp_lut=None, channel_size: int = 0,
+                  out_scale: int = 0, out_sigma: float = 0.0, out: torch.Tensor | None = None):
+    """Exact Requant of wide ciphertexts ``x`` [batch, elems, kN+1] (``pnb_requant_batch``);
+    ``shift``/``mult``/``round_bias`` are scalars (per-tensor) or per-channel sequences.
+    Returns (output ciphertexts, output TensorDesc)."""
+    import numpy as np
+    sh = np.atleast_1d(np.asarray(shift, dtype=np.uint32))
+    mu = np.atleast_1d(np.asarray(mult, dtype=np.uint64))
+    rb = np.atleast_1d(np.asarray(round_bias, dtype=np.uint64))
+    ch = len(sh)
+    if len(mu) != ch or len(rb) != ch:
+        raise ValueError("shift, mult and round_bias need one entry per channel")
+    lut = None if clamp_lut is None else np.ascontiguousarray(clamp_lut, dtype=np.uint64)
+
+    class Spec(C.Structure):
+        _fields_ = [("channels", C.c_int32), ("out_bits", C.c_int32),
+                    ("channel_size", C.c_int64), ("mult", C.c_void_p),
+                    ("round_bias", C.c_void_p), ("shift", C.c_void_p),
+                    ("clamp_lut", C.c_void_p)]
+
+    spec = Spec(ch, out_bits, channel_size, mu.ctypes.data, rb.ctypes.data, sh.ctypes.data,
+                None if lut is None else lut.ctypes.data)
+    return _op_call("pnb_requant_batch", ring, [C.byref(spec)], [desc], [x], desc.elems,
+                    out_scale, out_sigma, out)
+
+
+def argmax_batch(ring: KeyRing, x: torch.Tensor, desc: TensorDesc, threshold: int,
+                 out_scale: int = 0, out_sigma: float = 0.0, out: torch.Tensor | None = None):
+    """[v >= threshold] of a one-element tensor per sample (``pnb_argmax_batch``)."""
+    return _op_call("pnb_argmax_batch", ring, [C.c_int64(threshold)], [desc], [x], 1,
+                    out_scale, out_sigma, out)
+
+
+def add_batch(ring: KeyRing, a: torch.Tensor, da: TensorDesc, b: torch.Tensor, db: TensorDesc,
+              out_scale: int = 0, out_sigma: float = 0.0, out: torch.Tensor | None = None):
+    """a + b element-wise for tensors at one scale (``pnb_add_batch``)."""
+    return _op_call("pnb_add_batch", ring, [], [da, db], [a, b], da.elems, out_scale,
+                    out_sigma, out)

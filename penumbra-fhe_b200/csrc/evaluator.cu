@@ -6,6 +6,7 @@
 // are [sample][element][kN+1] u64 big-key LWE ciphertexts; the per-element tables (weights,
 // gather indices, linear-combination coefficients, test-vector choices) are uploaded once.
 #include <algorithm>
+#include <cmath>
 #include <cstring>
 #include <new>
 #include <string>
@@ -22,6 +23,13 @@ struct pnb_graph {
 struct pnb_plan {
   pnb::plan::Program prog;
   pnb_params params;
+};
+
+struct pnb_keyring {
+  int device = 0;
+  pnb_params params{};
+  std::vector<pnb::plan::KeyLevel> levels;  // the planner's key-set menu for params
+  std::vector<pnb_keys*> keys;              // one per level: same secret keys and KSK
 };
 
 namespace pnb {
@@ -115,6 +123,7 @@ struct pnb_evaluator {
   pnb::plan::Program prog;
   std::vector<pnb_keys*> keys;  // per program level (null when unused)
   pnb_keys* client = nullptr;   // the key set whose secret keys encrypt and decrypt
+  bool borrowed_keys = false;   // the keys belong to a key ring (pnb_evaluator_create_with)
   std::vector<pnb::DevInstr> dev;
   std::vector<void*> allocations;
   uint64_t* tvs = nullptr;  // [T][N]
@@ -268,6 +277,12 @@ int run_contract(pnb_evaluator* ev, size_t i, const plan::Instr& I, const DevIns
                                     ev->gathers[i], batch * I.P, ev->bufs[I.dst], L, I.P, st);
 }
 
+}  // namespace
+}  // namespace pnb
+
+namespace pnb {
+namespace {
+int evaluator_finish(pnb_evaluator* ev, const pnb_plan* p, size_t max_bytes);
 }  // namespace
 }  // namespace pnb
 
@@ -475,8 +490,9 @@ int pnb_evaluator_free(pnb_evaluator* ev) {
   free_chunk(ev);
   for (void* a : ev->allocations) cudaFree(a);
   cudaFree(ev->tvs);
-  for (pnb_keys* k : ev->keys)
-    if (k) pnb_keys_free(k);
+  if (!ev->borrowed_keys)
+    for (pnb_keys* k : ev->keys)
+      if (k) pnb_keys_free(k);
   delete ev;
   return PNB_OK;
 }
@@ -518,6 +534,121 @@ int pnb_evaluator_create(const pnb_plan* p, int device, uint64_t seed, size_t ma
     rc = pnb_keygen(device, &q, seed, &ev->keys[0]);
     ev->client = ev->keys[0];
   }
+  if (rc == PNB_OK) rc = evaluator_finish(ev, p, max_bytes);
+  if (rc != PNB_OK) {
+    pnb_evaluator_free(ev);
+    return rc;
+  }
+  *out = ev;
+  return PNB_OK;
+}
+
+int pnb_keyring_create(int device, const pnb_params* params, uint64_t seed, pnb_keyring** out) {
+  if (!params || !out) {
+    set_error("pnb_keyring_create: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  pnb_keyring* r = new (std::nothrow) pnb_keyring;
+  if (!r) {
+    set_error("pnb_keyring_create: out of host memory");
+    return PNB_ERR_OOM;
+  }
+  r->device = device;
+  r->params = *params;
+  r->levels = plan::default_levels(params->n, params->N, params->k, params->glwe_std);
+  r->keys.assign(r->levels.size(), nullptr);
+  int rc = PNB_OK;
+  for (size_t l = 0; l < r->levels.size() && rc == PNB_OK; ++l) {
+    pnb_params q = *params;
+    q.pbs_base_log = r->levels[l].base_log;
+    q.pbs_level = r->levels[l].level;
+    rc = pnb_keygen(device, &q, seed, &r->keys[l]);
+  }
+  if (rc != PNB_OK) {
+    pnb_keyring_free(r);
+    return rc;
+  }
+  *out = r;
+  return PNB_OK;
+}
+
+int pnb_keyring_free(pnb_keyring* r) {
+  if (!r) return PNB_OK;
+  for (pnb_keys* k : r->keys)
+    if (k) pnb_keys_free(k);
+  delete r;
+  return PNB_OK;
+}
+
+int pnb_keyring_keys(const pnb_keyring* r, int idx, pnb_keys** keys) {
+  if (!r || !keys || idx < 0 || idx >= (int)r->keys.size()) {
+    set_error("pnb_keyring_keys: bad argument (index %d of %d key sets)", idx,
+              r ? (int)r->keys.size() : 0);
+    return PNB_ERR_INVALID;
+  }
+  *keys = r->keys[idx];
+  return PNB_OK;
+}
+
+int pnb_evaluator_create_with(const pnb_plan* p, const pnb_keyring* ring, size_t max_bytes,
+                              pnb_evaluator** out) {
+  if (!p || !ring || !out) {
+    set_error("pnb_evaluator_create_with: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  const pnb_params& a = p->params;
+  const pnb_params& b = ring->params;
+  if (a.n != b.n || a.k != b.k || a.N != b.N || a.ks_base_log != b.ks_base_log ||
+      a.ks_level != b.ks_level || a.lwe_std != b.lwe_std || a.glwe_std != b.glwe_std) {
+    set_error("pnb_evaluator_create_with: the plan was compiled for another parameter set than "
+              "the key ring's");
+    return PNB_ERR_INVALID;
+  }
+  const auto& P = p->prog;
+  if (P.levels.size() != ring->levels.size()) {
+    set_error("pnb_evaluator_create_with: the plan's key-set menu differs from the key ring's");
+    return PNB_ERR_INVALID;
+  }
+  for (size_t l = 0; l < P.levels.size(); ++l)
+    if (P.levels[l].base_log != ring->levels[l].base_log ||
+        P.levels[l].level != ring->levels[l].level) {
+      set_error("pnb_evaluator_create_with: the plan's key-set menu differs from the key ring's");
+      return PNB_ERR_INVALID;
+    }
+  Guard guard(ring->device);
+  if (guard.rc) return guard.rc;
+  pnb_evaluator* ev = new (std::nothrow) pnb_evaluator;
+  if (!ev) {
+    set_error("pnb_evaluator_create_with: out of host memory");
+    return PNB_ERR_OOM;
+  }
+  ev->device = ring->device;
+  ev->params = p->params;
+  ev->prog = p->prog;
+  ev->keys = ring->keys;
+  ev->borrowed_keys = true;
+  ev->client = ring->keys[0];
+  int rc = evaluator_finish(ev, p, max_bytes);
+  if (rc != PNB_OK) {
+    pnb_evaluator_free(ev);
+    return rc;
+  }
+  *out = ev;
+  return PNB_OK;
+}
+
+}  // extern "C"
+
+namespace pnb {
+namespace {
+
+// Test vectors, per-instruction tables and the chunk limit of an evaluator whose key sets are
+// in place.
+int evaluator_finish(pnb_evaluator* ev, const pnb_plan* p, size_t max_bytes) {
+  const auto& P = ev->prog;
+  int rc = PNB_OK;
   // test vectors
   const int N = p->params.N;
   if (rc == PNB_OK && !P.tvs.empty()) {
@@ -587,13 +718,13 @@ int pnb_evaluator_create(const pnb_plan* p, int device, uint64_t seed, size_t ma
     ev->chunk_limit = (int)std::max<int64_t>(
         1, std::min<int64_t>(1 << 20, (int64_t)budget / std::max<int64_t>(per_sample, 1)));
   }
-  if (rc != PNB_OK) {
-    pnb_evaluator_free(ev);
-    return rc;
-  }
-  *out = ev;
-  return PNB_OK;
+  return rc;
 }
+
+}  // namespace
+}  // namespace pnb
+
+extern "C" {
 
 int pnb_evaluator_keys(const pnb_evaluator* ev, pnb_keys** keys) {
   if (!ev || !keys) {
@@ -663,6 +794,222 @@ int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t*
     }
   }
   return rc;
+}
+
+
+// ---- one op at a time ------------------------------------------------------------------------
+
+int pnb_op_plan_create(const char* op_json, size_t len, const pnb_params* p,
+                       const pnb_tensor_desc* in, int n_inputs, int out_scale_log2,
+                       double out_log2_sigma, double margin_sigmas, pnb_plan** out) {
+  if (!op_json || !p || !in || n_inputs < 1 || n_inputs > 2 || !out || out_scale_log2 < 0 ||
+      out_scale_log2 > 62 || out_log2_sigma < 0) {
+    set_error("pnb_op_plan_create: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  try {
+    // a one-node graph over inputs x0 (x1) -> y; the op payload is validated by the IR reader
+    std::string doc = "{\"schema_version\":\"";
+    doc += ir::SCHEMA_VERSION;
+    doc += "\",\"num_blocks\":31,\"input_bits\":1,\"inputs\":[\"x0\"";
+    if (n_inputs == 2) doc += ",\"x1\"";
+    doc += "],\"outputs\":[\"y\"],\"nodes\":[{\"name\":\"op\",\"inputs\":[\"x0\"";
+    if (n_inputs == 2) doc += ",\"x1\"";
+    doc += "],\"outputs\":[\"y\"],\"op\":";
+    doc.append(op_json, len);
+    doc += "}]}";
+    ir::Graph g = ir::parse_graph(doc.data(), doc.size());
+    for (const auto& n : g.nodes) ir::validate_op(n.op);
+    plan::Options o;
+    o.input_lo = in[0].lo;
+    o.input_hi = in[0].hi;
+    if (margin_sigmas > 0) o.z = margin_sigmas;
+    o.n = p->n;
+    o.N = p->N;
+    o.log2_ksms = plan::ksms_log2_sigma(p->n, p->N, p->k, p->ks_base_log, p->ks_level, p->lwe_std);
+    o.log2_fresh = std::log2(p->glwe_std) + 64;
+    o.levels = plan::default_levels(p->n, p->N, p->k, p->glwe_std);
+    o.check_budget = false;
+    o.output_scale = out_scale_log2;
+    o.output_log2_sigma = out_log2_sigma;
+    for (int i = 0; i < n_inputs; ++i) {
+      if (in[i].elems <= 0) {
+        set_error("pnb_op_plan_create: input %d has %lld elements", i, (long long)in[i].elems);
+        return PNB_ERR_INVALID;
+      }
+      o.input_lens.push_back(in[i].elems);
+      plan::InputSpec sp;
+      sp.scale = in[i].scale_log2;
+      sp.log2_sigma = in[i].log2_sigma;
+      sp.ranged = true;
+      sp.lo = in[i].lo;
+      sp.hi = in[i].hi;
+      o.input_specs.push_back(sp);
+    }
+    pnb_plan* pl = new pnb_plan;
+    try {
+      pl->prog = plan::build(g, o);
+    } catch (...) {
+      delete pl;
+      throw;
+    }
+    pl->params = *p;
+    *out = pl;
+    return PNB_OK;
+  } catch (const std::bad_alloc&) {
+    set_error("pnb_op_plan_create: out of host memory");
+    return PNB_ERR_OOM;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
+int pnb_plan_tensor_desc(const pnb_plan* p, int is_output, int idx, pnb_tensor_desc* d) {
+  if (!p || !d) {
+    set_error("pnb_plan_tensor_desc: NULL argument");
+    return PNB_ERR_INVALID;
+  }
+  const auto& v = is_output ? p->prog.outputs : p->prog.inputs;
+  if (idx < 0 || idx >= (int)v.size()) {
+    set_error("pnb_plan_tensor_desc: index %d out of range (%zu tensors)", idx, v.size());
+    return PNB_ERR_INVALID;
+  }
+  memset(d, 0, sizeof *d);
+  d->elems = v[idx].elems;
+  d->lo = v[idx].lo;
+  d->hi = v[idx].hi;
+  d->scale_log2 = v[idx].scale;
+  d->log2_sigma = v[idx].log2_sigma;
+  return PNB_OK;
+}
+
+}  // extern "C"
+
+namespace pnb {
+namespace {
+
+// Compile one op over `in`, bind it to the ring and run it on `batch` samples, packing several
+// inputs into the evaluator's [sample][input elements] layout.  Blocking.
+int run_one_op(const pnb_keyring* ring, const std::string& op_json, const pnb_tensor_desc* in,
+               const uint64_t* const* in_dev, int n_in, int batch, int out_scale,
+               double out_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc, cudaStream_t st,
+               const char* who) {
+  if (!ring || !in || !in_dev || !out_dev || batch < 0) {
+    set_error("%s: bad argument", who);
+    return PNB_ERR_INVALID;
+  }
+  for (int i = 0; i < n_in; ++i)
+    if (!in_dev[i] && batch > 0) {
+      set_error("%s: NULL input", who);
+      return PNB_ERR_INVALID;
+    }
+  pnb_plan* pl = nullptr;
+  int rc = pnb_op_plan_create(op_json.data(), op_json.size(), &ring->params, in, n_in,
+                              out_scale, out_sigma, 0, &pl);
+  if (rc) return rc;
+  if (out_desc) rc = pnb_plan_tensor_desc(pl, 1, 0, out_desc);
+  pnb_evaluator* ev = nullptr;
+  if (rc == PNB_OK) rc = pnb_evaluator_create_with(pl, ring, 0, &ev);
+  if (rc == PNB_OK && batch > 0) {
+    Guard guard(ring->device);
+    rc = guard.rc;
+    const int64_t L = row_words(ring->params);
+    const uint64_t* src = in_dev[0];
+    uint64_t* packed = nullptr;
+    if (rc == PNB_OK && n_in > 1) {
+      // [batch][e0 + e1][L] from the separate input tensors
+      int64_t tot = 0;
+      for (int i = 0; i < n_in; ++i) tot += in[i].elems;
+      cudaError_t e = cudaMallocAsync((void**)&packed, (size_t)batch * tot * L * 8, st);
+      if (e != cudaSuccess) rc = cuda_status(e, "cudaMallocAsync(op inputs)");
+      int64_t off = 0;
+      for (int i = 0; i < n_in && rc == PNB_OK; ++i) {
+        e = cudaMemcpy2DAsync(packed + off * L, (size_t)tot * L * 8, in_dev[i],
+                              (size_t)in[i].elems * L * 8, (size_t)in[i].elems * L * 8, batch,
+                              cudaMemcpyDeviceToDevice, st);
+        if (e != cudaSuccess) rc = cuda_status(e, "cudaMemcpy2DAsync(op inputs)");
+        off += in[i].elems;
+      }
+      src = packed;
+    }
+    if (rc == PNB_OK) rc = pnb_evaluate(ev, src, batch, out_dev, st);
+    if (packed) cudaFreeAsync(packed, st);
+    if (rc == PNB_OK) {
+      cudaError_t e = cudaStreamSynchronize(st);
+      if (e != cudaSuccess) rc = cuda_status(e, who);
+    }
+  }
+  pnb_evaluator_free(ev);
+  pnb_plan_free(pl);
+  return rc;
+}
+
+std::string u64_list(const uint64_t* v, int n) {
+  std::string s = "[";
+  for (int i = 0; i < n; ++i) s += (i ? "," : "") + std::to_string(v[i]);
+  return s + "]";
+}
+
+}  // namespace
+}  // namespace pnb
+
+extern "C" {
+
+int pnb_requant_batch(const pnb_keyring* ring, const pnb_requant_spec* spec,
+                      const pnb_tensor_desc* in, const uint64_t* in_dev, int batch,
+                      int out_scale_log2, double out_log2_sigma, uint64_t* out_dev,
+                      pnb_tensor_desc* out_desc, void* stream) {
+  if (!spec || !spec->mult || !spec->round_bias || !spec->shift || spec->channels < 1 ||
+      spec->out_bits < 1 || spec->out_bits > 16) {
+    set_error("pnb_requant_batch: bad requant spec");
+    return PNB_ERR_INVALID;
+  }
+  const int lut_n = 1 << spec->out_bits;
+  std::vector<uint64_t> lut((size_t)lut_n);
+  for (int i = 0; i < lut_n; ++i) lut[i] = spec->clamp_lut ? spec->clamp_lut[i] : (uint64_t)i;
+  std::string j = "{\"op_type\":\"Requant\",\"out_bits\":" + std::to_string(spec->out_bits) +
+                  ",\"clamp_lut\":" + u64_list(lut.data(), lut_n);
+  const int C = spec->channels;
+  if (C == 1) {
+    j += ",\"shift\":" + std::to_string(spec->shift[0]) + ",\"mult\":" +
+         std::to_string(spec->mult[0]) + ",\"round_bias\":" + std::to_string(spec->round_bias[0]);
+  } else {
+    std::vector<uint64_t> sh(spec->shift, spec->shift + C);
+    j += ",\"shift\":" + std::to_string(spec->shift[0]) + ",\"mults\":" +
+         u64_list(spec->mult, C) + ",\"round_biases\":" + u64_list(spec->round_bias, C) +
+         ",\"shifts\":" + u64_list(sh.data(), C) + ",\"channel_size\":" +
+         std::to_string(spec->channel_size);
+  }
+  j += "}";
+  const uint64_t* ins[1] = {in_dev};
+  return run_one_op(ring, j, in, ins, 1, batch, out_scale_log2, out_log2_sigma, out_dev,
+                    out_desc, (cudaStream_t)stream, "pnb_requant_batch");
+}
+
+int pnb_argmax_batch(const pnb_keyring* ring, int64_t threshold, const pnb_tensor_desc* in,
+                     const uint64_t* in_dev, int batch, int out_scale_log2,
+                     double out_log2_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc,
+                     void* stream) {
+  const std::string j = "{\"op_type\":\"Argmax\",\"threshold\":" + std::to_string(threshold) + "}";
+  const uint64_t* ins[1] = {in_dev};
+  return run_one_op(ring, j, in, ins, 1, batch, out_scale_log2, out_log2_sigma, out_dev,
+                    out_desc, (cudaStream_t)stream, "pnb_argmax_batch");
+}
+
+int pnb_add_batch(const pnb_keyring* ring, const pnb_tensor_desc* a, const uint64_t* a_dev,
+                  const pnb_tensor_desc* b, const uint64_t* b_dev, int batch, int out_scale_log2,
+                  double out_log2_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc,
+                  void* stream) {
+  if (!a || !b) {
+    set_error("pnb_add_batch: NULL descriptor");
+    return PNB_ERR_INVALID;
+  }
+  const pnb_tensor_desc d[2] = {*a, *b};
+  const uint64_t* ins[2] = {a_dev, b_dev};
+  return run_one_op(ring, "{\"op_type\":\"Add\"}", d, ins, 2, batch, out_scale_log2,
+                    out_log2_sigma, out_dev, out_desc, (cudaStream_t)stream, "pnb_add_batch");
 }
 
 }  // extern "C"

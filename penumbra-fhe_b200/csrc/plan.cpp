@@ -510,8 +510,12 @@ struct Builder {
   }
 
   // ---- top level ---------------------------------------------------------------------
+  const InputSpec* spec_of(size_t gi) const {
+    return gi < o.input_specs.size() ? &o.input_specs[gi] : nullptr;
+  }
+
   void run() {
-    ir::check_graph_bit_width_budget(g);
+    if (o.check_budget) ir::check_graph_bit_width_budget(g);
     for (size_t i = 0; i < o.levels.size(); ++i) lvl_order.push_back((int)i);
     std::sort(lvl_order.begin(), lvl_order.end(),
               [&](int a, int b) { return o.levels[a].cost < o.levels[b].cost; });
@@ -546,7 +550,10 @@ struct Builder {
       if (len < 0)
         fail("graph input '" + n + "' has no consumer that fixes its length (Linear, Conv2d, "
              "Pool or Argmax); pass its length explicitly");
-      range[tensor(n)].assign((size_t)len, Range{o.input_lo, o.input_hi});
+      const InputSpec* sp = spec_of(gi);
+      if (sp && sp->ranged && sp->lo > sp->hi) fail("graph input '" + n + "': empty value range");
+      range[tensor(n)].assign((size_t)len, sp && sp->ranged ? Range{sp->lo, sp->hi}
+                                                            : Range{o.input_lo, o.input_hi});
     }
     ranges();
     const int T = (int)tname.size();
@@ -586,6 +593,10 @@ struct Builder {
     std::vector<char> fresh(T, 0);
     for (int t = 0; t < T; ++t)
       if (producer[t] < 0) fresh[find(t)] = 1;
+    for (size_t gi = 0; gi < g.inputs.size(); ++gi) {
+      const InputSpec* sp = spec_of(gi);
+      if (sp && (sp->scale > 0 || sp->log2_sigma > 0)) fresh[find(tensor(g.inputs[gi]))] = 0;
+    }
     for (size_t ni = 0; ni < g.nodes.size(); ++ni) {
       const auto& op = g.nodes[ni].op;
       const int yt = tensor(g.nodes[ni].inputs[0]);
@@ -606,6 +617,25 @@ struct Builder {
       }
       if (zlo > -((i128)1 << 56) && zhi < ((i128)1 << 56)) tighten(yt, (int64_t)zlo, (int64_t)zhi);
     }
+    // scales the caller pins: inputs arriving from earlier ops, outputs feeding later ones
+    std::vector<int> forced(T, 0);
+    auto force = [&](int t, int s, const std::string& what) {
+      const int c = find(t);
+      if (s > cap[c])
+        fail(what + " at scale 2^" + std::to_string(s) + " leaves no room for the values it " +
+             "must hold (at most 2^" + std::to_string(cap[c]) + ")");
+      if (forced[c] && forced[c] != s)
+        fail(what + ": scales 2^" + std::to_string(forced[c]) + " and 2^" + std::to_string(s) +
+             " meet where one encoding is needed");
+      forced[c] = s;
+      cap[c] = s;
+    };
+    for (size_t gi = 0; gi < g.inputs.size(); ++gi) {
+      const InputSpec* sp = spec_of(gi);
+      if (sp && sp->scale > 0) force(tensor(g.inputs[gi]), sp->scale, "graph input '" + g.inputs[gi] + "'");
+    }
+    if (o.output_scale > 0)
+      for (const auto& n : g.outputs) force(tensor(n), o.output_scale, "graph output '" + n + "'");
     for (int t = 0; t < T; ++t) {
       scale[t] = cap[find(t)];
       if (scale[t] < 8)
@@ -617,6 +647,7 @@ struct Builder {
       const int t = tensor(n);
       const double h = std::ldexp(1.0, scale[t] - 1) / o.z;
       vmax[t] = std::min(vmax[t], h * h);
+      if (o.output_log2_sigma > 0) vmax[t] = std::min(vmax[t], std::exp2(2 * o.output_log2_sigma));
     }
     for (int ni = (int)g.nodes.size() - 1; ni >= 0; --ni) {
       const auto& nd = g.nodes[ni];
@@ -668,22 +699,28 @@ struct Builder {
     P.opt = o;
     P.levels = o.levels;
     int64_t in_off = 0;
-    for (const auto& n : g.inputs) {
+    for (size_t gi = 0; gi < g.inputs.size(); ++gi) {
+      const std::string& n = g.inputs[gi];
       const int t = tensor(n);
+      const InputSpec* sp = spec_of(gi);
       buf[t] = new_buf((int64_t)range[t].size(), n);
-      const double s = std::exp2(o.log2_fresh);
+      const double ls = sp && sp->log2_sigma > 0 ? sp->log2_sigma : o.log2_fresh;
+      const double s = std::exp2(ls);
       var[t] = s * s;
       TensorIO io;
       io.name = n;
       io.buf = buf[t];
       io.elems = (int64_t)range[t].size();
       io.scale = scale[t];
-      io.log2_sigma = o.log2_fresh;
-      io.lo = o.input_lo;
-      io.hi = o.input_hi;
+      io.log2_sigma = ls;
+      io.lo = sp && sp->ranged ? sp->lo : o.input_lo;
+      io.hi = sp && sp->ranged ? sp->hi : o.input_hi;
       P.inputs.push_back(io);
       in_off += io.elems;
-      if (var[t] > vmax[t]) fail("graph input noise exceeds what its consumers tolerate");
+      if (var[t] > vmax[t])
+        fail("graph input '" + n + "': noise 2^" + std::to_string(ls) + " at scale 2^" +
+             std::to_string(scale[t]) + " exceeds what its consumers tolerate (2^" +
+             std::to_string(0.5 * std::log2(vmax[t])) + ")");
     }
     P.input_elems = in_off;
     std::ostringstream rep;

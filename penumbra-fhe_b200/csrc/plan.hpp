@@ -44,8 +44,21 @@ struct KeyLevel {
   double cost = 1.0;         // relative time of one bootstrap
 };
 
+// What the caller knows about one graph input when it is not a fresh client encryption (the
+// output of an earlier op, evaluated one op at a time).
+struct InputSpec {
+  int scale = 0;          // plaintext scale (log2) the ciphertexts carry; 0 = the planner's choice
+  double log2_sigma = 0;  // noise std (log2, torus units); 0 = a fresh encryption
+  bool ranged = false;    // lo/hi below bound the values (otherwise input_lo / input_hi)
+  int64_t lo = 0, hi = 0;
+};
+
 struct Options {
   int64_t input_lo = 0, input_hi = 0;  // declared range of every graph-input element
+  std::vector<InputSpec> input_specs;  // per graph input (absent entries: defaults)
+  int output_scale = 0;                // scale (log2) of every graph output; 0 = planner's choice
+  double output_log2_sigma = 0;        // noise bound (log2 std) of every graph output; 0 = none
+  bool check_budget = true;            // the reference's radix bit-width budget (whole graphs)
   double z = 7.0;                      // decision margin in standard deviations
   int n = 834, N = 2048;
   double log2_ksms = 54.83;   // keyswitch + modulus-switch noise std at the rotation input
