@@ -321,6 +321,26 @@ int pnb_op_plan_create(const char* op_json, size_t len, const pnb_params* params
                        const pnb_tensor_desc* in, int n_inputs, int out_scale_log2,
                        double out_log2_sigma, double margin_sigmas, pnb_plan** out);
 int pnb_plan_tensor_desc(const pnb_plan* plan, int is_output, int idx, pnb_tensor_desc* desc);
+/* Conversion programs between wide ciphertexts and the reference's radix blocks (one block per
+ * msg_bits digit, two's complement when is_signed, block 0 least significant, each block a
+ * big-key ciphertext of its digit at the block scale 2^(63 - msg_bits - carry_bits), laid out
+ * [element][num_blocks]).  Run them with an evaluator like any plan.
+ *   to_blocks = 1 (split): `wide` describes the input integers (elems, value range, scale,
+ *     noise); the output holds elems * num_blocks clean blocks.  Four bootstraps per digit
+ *     (three for the top one): the digits are peeled off LSB first, each window read through the
+ *     negacyclic sign and a two-box lookup, with the key sets that keep every later read exact.
+ *   to_blocks = 0 (merge): the input holds elems * num_blocks blocks whose digits reach at most
+ *     block_max (0: clean blocks, digits below 2^msg_bits, as encrypt_signed and every
+ *     carry-propagating radix op leave them; up to 2^(msg_bits + carry_bits) - 1 with carries,
+ *     which widens the integer); `wide` requests the output: elems, scale (0: the widest that holds the
+ *     integers) and a noise bound (log2_sigma; 0: decodable with the margin).  One bootstrap per
+ *     block, with the cheapest key set whose summed outputs meet the bound, then a sum.
+ * Replaces: RadixClientKey::encrypt_signed / decrypt_signed's block encoding at graph
+ * boundaries (runtime/src/encrypt.rs:20-22, 43-45; SignedRadixCiphertext,
+ * runtime/src/ops/mod.rs:58). */
+int pnb_radix_plan_create(const pnb_params* params, int num_blocks, int is_signed, int to_blocks,
+                          int block_max, const pnb_tensor_desc* wide, double margin_sigmas,
+                          pnb_plan** out);
 /* An evaluator of `plan` that borrows the ring's key sets (no key generation) on the ring's
  * device.  The ring must outlive the evaluator. */
 int pnb_evaluator_create_with(const pnb_plan* plan, const pnb_keyring* ring, size_t max_bytes,

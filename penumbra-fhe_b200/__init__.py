@@ -23,6 +23,7 @@ __all__ = [
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
     "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys", "radix_merge",
     "TensorDesc", "KeyRing", "op_plan", "requant_batch", "argmax_batch", "add_batch",
+    "radix_plan",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -127,6 +128,8 @@ _SIGS = {
                                      C.c_int, C.c_int, C.c_double, C.c_double,
                                      C.POINTER(C.c_void_p)]),
     "pnb_plan_tensor_desc": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "pnb_radix_plan_create": (C.c_int, [C.POINTER(Params), C.c_int, C.c_int, C.c_int, C.c_int,
+                                        C.c_void_p, C.c_double, C.POINTER(C.c_void_p)]),
     "pnb_evaluator_create_with": (C.c_int, [C.c_void_p, C.c_void_p, C.c_size_t,
                                             C.POINTER(C.c_void_p)]),
     "pnb_requant_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
@@ -812,6 +815,21 @@ def op_plan(op: dict, inputs: list[TensorDesc], params: Params | None = None,
            lib().pnb_op_plan_create(text, len(text), C.byref(params), C.cast(arr, C.c_void_p),
                                     len(inputs), out_scale, out_sigma, margin_sigmas,
                                     C.byref(h)))
+    pl = Plan.__new__(Plan)
+    pl._init_from_handle(h, params)
+    return pl
+
+
+def radix_plan(num_blocks: int, wide: TensorDesc, to_blocks: bool, signed: bool = True,
+               block_max: int = 0, params: Params | None = None,
+               margin_sigmas: float = 0.0) -> Plan:
+    """Radix split (``to_blocks``) or merge program (``pnb_radix_plan_create``)."""
+    params = default_params() if params is None else params
+    h = C.c_void_p()
+    _check("pnb_radix_plan_create",
+           lib().pnb_radix_plan_create(C.byref(params), num_blocks, int(bool(signed)),
+                                       int(bool(to_blocks)), block_max, C.byref(wide),
+                                       margin_sigmas, C.byref(h)))
     pl = Plan.__new__(Plan)
     pl._init_from_handle(h, params)
     return pl

@@ -866,6 +866,54 @@ int pnb_op_plan_create(const char* op_json, size_t len, const pnb_params* p,
   }
 }
 
+int pnb_radix_plan_create(const pnb_params* p, int num_blocks, int is_signed, int to_blocks,
+                          int block_max, const pnb_tensor_desc* wide, double margin_sigmas,
+                          pnb_plan** out) {
+  if (!p || !wide || !out || num_blocks < 1 || wide->elems < 1) {
+    set_error("pnb_radix_plan_create: bad argument");
+    return PNB_ERR_INVALID;
+  }
+  *out = nullptr;
+  try {
+    plan::Options o;
+    if (margin_sigmas > 0) o.z = margin_sigmas;
+    o.n = p->n;
+    o.N = p->N;
+    o.log2_ksms = plan::ksms_log2_sigma(p->n, p->N, p->k, p->ks_base_log, p->ks_level, p->lwe_std);
+    o.log2_fresh = std::log2(p->glwe_std) + 64;
+    o.levels = plan::default_levels(p->n, p->N, p->k, p->glwe_std);
+    plan::RadixSpec r;
+    r.to_blocks = to_blocks != 0;
+    r.is_signed = is_signed != 0;
+    r.num_blocks = num_blocks;
+    r.msg_bits = p->msg_bits;
+    r.carry_bits = p->carry_bits;
+    r.block_max = block_max;
+    r.elems = wide->elems;
+    r.wide.scale = wide->scale_log2;
+    r.wide.log2_sigma = wide->log2_sigma;
+    r.wide.ranged = true;
+    r.wide.lo = wide->lo;
+    r.wide.hi = wide->hi;
+    pnb_plan* pl = new pnb_plan;
+    try {
+      pl->prog = plan::build_radix(r, o);
+    } catch (...) {
+      delete pl;
+      throw;
+    }
+    pl->params = *p;
+    *out = pl;
+    return PNB_OK;
+  } catch (const std::bad_alloc&) {
+    set_error("pnb_radix_plan_create: out of host memory");
+    return PNB_ERR_OOM;
+  } catch (const std::exception& e) {
+    set_error("%s", e.what());
+    return PNB_ERR_INVALID;
+  }
+}
+
 int pnb_plan_tensor_desc(const pnb_plan* p, int is_output, int idx, pnb_tensor_desc* d) {
   if (!p || !d) {
     set_error("pnb_plan_tensor_desc: NULL argument");

@@ -1229,6 +1229,199 @@ struct Builder {
     rep << line;
   }
 
+  // ---- radix conversion ------------------------------------------------------------
+  void setup_levels() {
+    for (size_t i = 0; i < o.levels.size(); ++i) lvl_order.push_back((int)i);
+    std::sort(lvl_order.begin(), lvl_order.end(),
+              [&](int a, int b) { return o.levels[a].cost < o.levels[b].cost; });
+    if (o.levels.empty()) fail("no bootstrap key sets given");
+    V_ksms = std::exp2(2 * o.log2_ksms);
+    P.opt = o;
+    P.levels = o.levels;
+  }
+
+  TensorIO io_of(int b, const std::string& name, int64_t elems, int sc, double v, int64_t lo,
+                 int64_t hi) {
+    TensorIO io;
+    io.name = name;
+    io.buf = b;
+    io.elems = elems;
+    io.scale = sc;
+    io.log2_sigma = 0.5 * std::log2(std::max(v, 1.0));
+    io.lo = lo;
+    io.hi = hi;
+    return io;
+  }
+
+  // wide -> blocks: LSB-first, every digit's 2-bit window is read twice (its top bit through the
+  // negacyclic sign, then the low bit by a two-box lookup); each read runs once at the wide
+  // value's scale, whose outputs clear the digit from the running value, and once at the block
+  // scale, whose outputs form the block.
+  void run_split(const RadixSpec& r) {
+    setup_levels();
+    const int nb = r.num_blocks, mb = r.msg_bits;
+    if (mb != 2) fail("radix split: blocks of " + std::to_string(mb) + " message bits are not "
+                      "supported (the reference's blocks carry 2)");
+    const int64_t E = r.elems;
+    const int eb = 63 - r.msg_bits - r.carry_bits;  // block scale
+    const InputSpec& w = r.wide;
+    const int width = mb * nb;
+    if (r.is_signed ? (w.lo < -((i128)1 << (width - 1)) || w.hi >= ((i128)1 << (width - 1)))
+                    : (w.lo < 0 || w.hi >= ((i128)1 << width)))
+      fail("radix split: values in [" + std::to_string(w.lo) + ", " + std::to_string(w.hi) +
+           "] do not fit " + std::to_string(nb) + (r.is_signed ? " signed" : " unsigned") +
+           " 2-bit blocks");
+    const int s_in = w.scale;
+    if (s_in < 1 || s_in + width > 64)
+      fail("radix split: input scale 2^" + std::to_string(s_in) + " leaves no room for " +
+           std::to_string(width) + " bits");
+    const double v_in = std::exp2(2 * (w.log2_sigma > 0 ? w.log2_sigma : o.log2_fresh));
+    // key sets of the clearing reads: every read of window i must see noise below its budget
+    Chain c{-1, -1, E, s_in, v_in};
+    std::vector<int> ws(nb, 2), lv;
+    double Vend = 0, cost = 0;
+    if (!eval_windows(c, ws, 64, &lv, &Vend, &cost))
+      fail("radix split: the input's noise (2^" + std::to_string(0.5 * std::log2(v_in)) +
+           ") at scale 2^" + std::to_string(s_in) + " is too large to read its digits exactly");
+    const int l0 = lvl_order[0];
+    // block outputs are read by the reference's own bootstraps: keep them well inside a cell
+    const double blk_lim = std::pow(std::ldexp(1.0, eb - 1) / o.z, 2);
+    if (2 * lvar(l0) > blk_lim) fail("radix split: the cheapest key set is too noisy for blocks");
+    const int IN = new_buf(E, "wide");
+    const int R = new_buf(E, "running");
+    const int Xc = new_buf(E, "clear");
+    const int Xb = new_buf(E, "block bit");
+    const int Yb = new_buf(E, "block low bit");
+    const int OUT = new_buf(E * nb, "blocks");
+    P.inputs.push_back(io_of(IN, "wide", E, s_in, v_in, w.lo, w.hi));
+    lin(R, {Term{IN, {1}, {}}}, {0}, "split: running value");
+    double V = v_in;
+    for (int i = 0; i < nb; ++i) {
+      const int Ei = s_in + 2 * i;
+      const int shift = 62 - Ei;
+      const bool top = i == nb - 1;
+      const std::string at = "digit " + std::to_string(i);
+      // top bit of the window: +C (0) or -C (1) at the running scale and at the block scale
+      pbs(Xc, R, shift, pow2(61), lv[2 * i], {tv(const_tv(pow2(Ei)))}, E, at + ": sign (clear)");
+      pbs(Xb, R, shift, pow2(61), l0, {tv(const_tv(pow2(eb)))}, E, at + ": sign (block)");
+      lin(R, {Term{R, {1}, {}}, Term{Xc, {1}, {}}}, {(uint64_t)0 - pow2(Ei)}, at + ": clear top");
+      V += lvar(lv[2 * i]);
+      // low bit of the window
+      TvSpec lb;
+      lb.lut_len = 2;
+      lb.val = {0, pow2(eb)};
+      pbs(Yb, R, shift, 0, l0, {tv(lb)}, E, at + ": low bit (block)");
+      // block i = (2^eb - Xb) + Yb = (2 b1 + b0) 2^eb
+      std::vector<int32_t> map(E * nb, -1);
+      for (int64_t e = 0; e < E; ++e) map[e * nb + i] = (int32_t)e;
+      std::vector<uint64_t> cst(E * nb, 0);
+      for (int64_t e = 0; e < E; ++e) cst[e * nb + i] = pow2(eb);
+      if (i == 0) {
+        lin(OUT, {Term{Xb, {-1}, map}, Term{Yb, {1}, map}}, cst, at + ": block");
+      } else {
+        std::vector<int32_t> id(E * nb);
+        for (int64_t q = 0; q < E * nb; ++q) id[q] = (int32_t)q;
+        lin(OUT, {Term{OUT, {1}, id}, Term{Xb, {-1}, map}, Term{Yb, {1}, map}}, cst,
+            at + ": block");
+      }
+      if (!top) {
+        TvSpec lc;
+        lc.lut_len = 2;
+        lc.val = {0, pow2(Ei)};
+        pbs(Xc, R, shift, 0, lv[2 * i + 1], {tv(lc)}, E, at + ": low bit (clear)");
+        lin(R, {Term{R, {1}, {}}, Term{Xc, {-1}, {}}}, {0}, at + ": clear low");
+        V += lvar(lv[2 * i + 1]);
+      }
+    }
+    P.input_elems = E;
+    P.outputs.push_back(io_of(OUT, "blocks", E * nb, eb, 2 * lvar(l0), 0, 3));
+    P.output_elems = E * nb;
+    std::ostringstream rep;
+    rep << "radix split: " << E << " integers -> " << nb << " blocks each, "
+        << P.pbs_per_sample / std::max<int64_t>(E, 1) << " bootstraps per integer\n";
+    P.report = rep.str();
+  }
+
+  // blocks -> wide: one lookup per block, d -> its weighted digit at the output scale, summed.
+  void run_merge(const RadixSpec& r) {
+    setup_levels();
+    const int nb = r.num_blocks, mb = r.msg_bits, space = 1 << (r.msg_bits + r.carry_bits);
+    const int64_t E = r.elems;
+    const int eb = 63 - r.msg_bits - r.carry_bits;
+    const int dmax = r.block_max > 0 ? r.block_max : (1 << mb) - 1;
+    if (dmax >= space) fail("radix merge: a block holds digits below " + std::to_string(space));
+    if ((int64_t)nb * mb > 62) fail("radix merge: too many blocks for a 64-bit torus");
+    // value range of the merged integer
+    i128 lo = 0, hi = 0;
+    for (int i = 0; i < nb; ++i) {
+      const i128 wgt = (i128)1 << (mb * i);
+      if (r.is_signed && i == nb - 1) {
+        lo += -(i128)(1 << (mb - 1)) * wgt;
+        hi += (i128)((1 << (mb - 1)) - 1) * wgt;
+      } else {
+        hi += (i128)dmax * wgt;
+      }
+    }
+    const int cap = 63 - bits_signed(to_i64(lo, "radix merge"), to_i64(hi, "radix merge"));
+    const int so = r.wide.scale > 0 ? r.wide.scale : cap;
+    if (so > cap)
+      fail("radix merge: output scale 2^" + std::to_string(so) + " leaves no room for " +
+           std::to_string(nb * mb) + "-bit integers (at most 2^" + std::to_string(cap) + ")");
+    double vmax_out = std::pow(std::ldexp(1.0, so - 1) / o.z, 2);
+    if (r.wide.log2_sigma > 0) vmax_out = std::min(vmax_out, std::exp2(2 * r.wide.log2_sigma));
+    int lvl = -1;
+    for (int l : lvl_order)
+      if (nb * lvar(l) <= vmax_out) {
+        lvl = l;
+        break;
+      }
+    if (lvl < 0)
+      fail("radix merge: " + std::to_string(nb) + " blocks sum " + std::to_string(nb) +
+           " bootstrap outputs, and no key set keeps that sum below 2^" +
+           std::to_string(0.5 * std::log2(vmax_out)) + " (scale 2^" + std::to_string(so) + ")");
+    const double v_blk = std::max(std::exp2(2 * o.log2_fresh), lvar(lvl_order[0]));
+    if (v_blk > allowed(eb, eb)) fail("radix merge: block noise too large to read");
+    const int IN = new_buf(E * nb, "blocks");
+    const int X = new_buf(E * nb, "weighted");
+    const int OUT = new_buf(E, "wide");
+    P.inputs.push_back(io_of(IN, "blocks", E * nb, eb, v_blk, 0, dmax));
+    std::vector<int32_t> tvi(E * nb);
+    std::vector<int> tv_of(nb);
+    for (int i = 0; i < nb; ++i) {
+      TvSpec sp;
+      sp.lut_len = space;
+      const i128 wgt = (i128)1 << (mb * i);
+      for (int d = 0; d < space; ++d) {
+        i128 v = (i128)d * wgt;
+        if (r.is_signed && i == nb - 1) {
+          const int dm = d % (1 << mb);
+          v = (i128)(dm >= (1 << (mb - 1)) ? dm - (1 << mb) : dm) * wgt;
+        }
+        sp.val.push_back((uint64_t)(int64_t)v << so);
+      }
+      tv_of[i] = tv(sp);
+    }
+    for (int64_t q = 0; q < E * nb; ++q) tvi[q] = tv_of[q % nb];
+    pbs(X, IN, 0, 0, lvl, tvi, E * nb, "merge: weighted digits");
+    for (int i0 = 0; i0 < nb; i0 += 3) {
+      std::vector<Term> terms;
+      if (i0 > 0) terms.push_back(Term{OUT, {1}, {}});
+      for (int i = i0; i < std::min(nb, i0 + 3); ++i) {
+        std::vector<int32_t> map(E);
+        for (int64_t e = 0; e < E; ++e) map[e] = (int32_t)(e * nb + i);
+        terms.push_back(Term{X, {1}, map});
+      }
+      lin(OUT, terms, {0}, "merge: sum of blocks");
+    }
+    P.input_elems = E * nb;
+    P.outputs.push_back(io_of(OUT, "wide", E, so, nb * lvar(lvl), (int64_t)lo, (int64_t)hi));
+    P.output_elems = E;
+    std::ostringstream rep;
+    rep << "radix merge: " << nb << " blocks -> 1 integer at 2^" << so << ", " << nb
+        << " bootstraps with key " << key_name(lvl) << "\n";
+    P.report = rep.str();
+  }
+
   // Final sign read of every pair, then either
   //  (direct)   out = base + sum_j delta_j [v_j >= 0], each sign bootstrap emitting its term at
   //             the output scale with the key the output's consumers need, or
@@ -1361,6 +1554,15 @@ Program build(const ir::Graph& g, const Options& o) {
   }
   if (!have) throw Error(first_error);
   return best;
+}
+
+Program build_radix(const RadixSpec& r, const Options& o) {
+  static const ir::Graph empty;
+  if (r.num_blocks < 1 || r.elems < 1) throw Error("radix program: need blocks and elements");
+  Builder b(empty, o);
+  if (r.to_blocks) b.run_split(r);
+  else b.run_merge(r);
+  return std::move(b.P);
 }
 
 // ---- noise-free execution ------------------------------------------------------------

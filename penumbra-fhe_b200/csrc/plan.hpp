@@ -131,6 +131,25 @@ struct Program {
 // bit-width budget, uses an op this path does not implement, or no exact plan exists.
 Program build(const ir::Graph& g, const Options& o);
 
+// Radix conversion programs between wide ciphertexts and the reference's radix blocks (one
+// block per msg_bits digit of the integer, two's complement when is_signed, at the block scale
+// 2^(63 - msg_bits - carry_bits); block 0 least significant).
+//   split (to_blocks): input `wide` (elems integers at wide.scale with wide.log2_sigma noise,
+//          values in [wide.lo, wide.hi]); output elems * num_blocks clean blocks, element-major.
+//   merge: input elems * num_blocks blocks (digits up to block_max: clean, or with carries up
+//          to the block space; fresh or bootstrapped); output elems integers at wide.scale (0: the widest that holds them)
+//          with noise below wide.log2_sigma (0: decodable with the margin).
+struct RadixSpec {
+  bool to_blocks = true;
+  bool is_signed = true;
+  int num_blocks = 1;
+  int msg_bits = 2, carry_bits = 2;
+  int block_max = 0;  // merge: largest digit a block may hold (0: clean, 2^msg_bits - 1)
+  int64_t elems = 1;
+  InputSpec wide;
+};
+Program build_radix(const RadixSpec& r, const Options& o);
+
 // Noise-free execution: inputs [batch][input_elems] integers, outputs [batch][output_elems]
 // decoded integers.  min_margin receives the smallest distance (in units of 2^64/2N) between a
 // bootstrap's exact input phase and the nearest boundary where its test vector changes value.
