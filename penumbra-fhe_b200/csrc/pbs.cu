@@ -735,9 +735,11 @@ static int launch_ml_any(const pnb_keys* K, TvSel tv, const uint64_t* small, uin
 static bool br_supported(const pnb_params& p) {
   if (p.k != 1 || p.N != FFT_N || p.n > BR_MAXN || p.n <= 0) return false;
   if (p.pbs_level == 1) return p.pbs_base_log >= 2 && p.pbs_base_log <= 30;
-  // multi-level: digits below 2^22 in magnitude keep the f64 product's error small
+  // multi-level: digits below 2^22 in magnitude keep the f64 product's error small, and the
+  // 48-bit accumulator holds the digits' T = base_log * level bits plus the rounding bit
+  if (p.pbs_level == 9) return p.pbs_base_log == 5;
   return p.pbs_level >= 2 && p.pbs_level <= 6 && p.pbs_base_log >= 2 &&
-         p.pbs_base_log <= 22 && p.pbs_base_log * p.pbs_level < 64;
+         p.pbs_base_log <= 22 && p.pbs_base_log * p.pbs_level <= 46;
 }
 
 int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
@@ -753,7 +755,8 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
   }
   const TvSel tv{tvs, tv_idx, period, tv_idx ? first % period : 0};
   if (!br_supported(K->p)) {
-    set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level 1..6, n<=%d (got "
+    set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level 1..6 and (2^5, 9), "
+              "n<=%d (got "
               "k=%d N=%d level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
               K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
@@ -769,6 +772,7 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
     case 4: return launch_ml_any<4, 10>(K, tv, small, out, count, tb, st);
     case 5: return launch_ml_any<5, 8>(K, tv, small, out, count, tb, st);
     case 6: return launch_ml_any<6, 7>(K, tv, small, out, count, tb, st);
+    case 9: return launch_mlb<9, 5>(K, tv, small, out, count, tb, st);
     default:
       set_error("blind rotation: pbs_level %d not compiled", K->p.pbs_level);
       return PNB_ERR_UNSUPPORTED;
@@ -794,7 +798,8 @@ size_t pbs_workspace_bytes(const pnb_keys* K, int count) {
 int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
               int count, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!br_supported(K->p)) {
-    set_error("pbs: compiled kernels cover k=1, N=2048, pbs_level 1..6, n<=%d (got k=%d N=%d "
+    set_error("pbs: compiled kernels cover k=1, N=2048, pbs_level 1..6 and (2^5, 9), n<=%d (got "
+              "k=%d N=%d "
               "level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
               K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;

@@ -112,3 +112,34 @@ def test_merge_22bit_integers_with_a_multilevel_key_set(pnb):
     assert np.array_equal(got, v)
     assert np.log2(err.astype(np.float64).std()) < 36.5
     assert pnb.device_status(0) == 0
+
+
+@pytest.fixture(scope="module")
+def ring(pnb):
+    return pnb.KeyRing(seed=SEED, device=0)
+
+
+@pytest.mark.parametrize("nb", [4, 12])
+def test_split_merge_round_trip_encrypted(pnb, ring, nb):
+    # wide signed integers -> the reference's 2-bit radix blocks -> wide again, exactly; 12
+    # blocks (24-bit integers) is the widest merge whose summed block noise the lowest-noise
+    # key set keeps 7 sigma inside a cell
+    lo, hi = -(1 << (2 * nb - 1)), (1 << (2 * nb - 1)) - 1
+    scale = 62 - 2 * nb
+    rng = np.random.default_rng(SEED + nb)
+    count = 64
+    v = rng.integers(lo, hi + 1, count)
+    v[:4] = [lo, hi, 0, -1]
+    split = pnb.radix_plan(nb, pnb.TensorDesc.make(count, lo, hi, scale), to_blocks=True)
+    merge = pnb.radix_plan(nb, pnb.TensorDesc.make(count, 0, 0), to_blocks=False)
+    ev_s = pnb.Evaluator(split, ring=ring)
+    ev_m = pnb.Evaluator(merge, ring=ring)
+    wide = ring.encrypt(v.reshape(1, count), scale, seed=SEED + 40 + nb)
+    blocks = ev_s.evaluate(wide)                       # [1][count * nb][kN+1]
+    digits = ring.decrypt(blocks, 59).cpu().numpy().reshape(count, nb)
+    u = v & ((1 << (2 * nb)) - 1)
+    assert np.array_equal(digits, np.stack([(u >> (2 * i)) & 3 for i in range(nb)], axis=1))
+    back = ev_m.evaluate(blocks)
+    got = ring.decrypt(back, merge.desc(True).scale_log2).cpu().numpy().reshape(-1)
+    assert np.array_equal(got, v)
+    assert pnb.device_status(0) == 0
