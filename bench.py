@@ -287,7 +287,7 @@ def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 6
     return out
 
 
-def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6)), B=4096):
+def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6), (5, 9)), B=4096):
     """PBS/s of the multi-level key sets the graph planner uses (keyswitch + blind rotation,
     device-timed at batch B, L2 flushed between repetitions), each checked by decryption."""
     import numpy as np

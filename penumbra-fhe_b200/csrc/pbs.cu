@@ -385,6 +385,245 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
 constexpr int BR_CPB = 4;
 
 // ------------------------------------------------------------------------------------------
+// The same blind rotation with the twiddles and the pair exchange in tensor memory.
+//
+// Shared memory serves every other stream of the CMux (digit formation, the two transposes, the
+// key rows, the accumulator update); the forward and inverse twiddles (16 KB per warp and
+// transform) and the exchange of the two warps' spectra (32 KB per warp and CMux) go through
+// tensor memory instead, a third less shared-memory traffic.  Warp w owns polynomial
+// p = w / 4 of ciphertext c = w % 4, so the two warps of a ciphertext share lane quarter c of
+// tensor memory.  Columns (per lane quarter, lane l): [0, 128) forward twiddles T(r, l) for
+// r = 0..31 as (re lo, re hi, im lo, im hi) words; [128, 256) T(l, n) for n = 0..31 (the inverse
+// multiplies by their conjugates); [256, 384) and [384, 512) the spectra of the mask and body
+// warps.
+// ------------------------------------------------------------------------------------------
+template <int CPB>
+struct BrTmLayout {
+  static constexpr int WARPS = 2 * CPB;
+  static constexpr int SCRATCH = FFT_M * sizeof(double);            // 8 KB per warp
+  static constexpr int ACC = FFT_N * sizeof(uint32_t);              // 8 KB per warp
+  static constexpr int BSK = 4 * FFT_M * sizeof(double2);           // 64 KB: one GGSW (k=1,l=1)
+  static constexpr int ABAR = BR_MAXN * sizeof(uint16_t);           // 2 KB per ciphertext
+  static constexpr int OFF_ACC = WARPS * SCRATCH;
+  static constexpr int OFF_BSK = OFF_ACC + WARPS * ACC;
+  static constexpr int OFF_ABAR = OFF_BSK + BSK;
+  static constexpr int OFF_BAR = OFF_ABAR + CPB * ABAR;  // mbarrier, abort flag, TMEM base
+  static constexpr int BYTES = OFF_BAR + 16;
+  static constexpr int TMEM_COLS = 512;
+};
+
+__device__ __forceinline__ void d2_to_words(double2 v, uint32_t* t) {
+  t[0] = (uint32_t)__double2loint(v.x);
+  t[1] = (uint32_t)__double2hiint(v.x);
+  t[2] = (uint32_t)__double2loint(v.y);
+  t[3] = (uint32_t)__double2hiint(v.y);
+}
+__device__ __forceinline__ double2 words_to_d2(const uint32_t* t) {
+  return make_double2(__hiloint2double((int)t[1], (int)t[0]),
+                      __hiloint2double((int)t[3], (int)t[2]));
+}
+
+template <int CPB>
+__global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
+    const uint64_t* __restrict__ small_ct, TvSel sel,
+    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
+    int base_log, FftTables tb) {
+  static_assert(CPB == 4, "the lane-quarter mapping needs four ciphertexts per block");
+  using L = BrTmLayout<CPB>;
+  extern __shared__ __align__(128) unsigned char bt_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int cl = warp & 3, p = warp >> 2;
+  const int ct = blockIdx.x * CPB + cl;
+  const bool valid = ct < count;
+  constexpr int LG = 12;  // log2(2N)
+  double* buf = reinterpret_cast<double*>(bt_raw) + warp * FFT_M;
+  uint2* acc2 = reinterpret_cast<uint2*>(bt_raw + L::OFF_ACC) + warp * FFT_M;
+  auto acc_at = [&](int e) { return e < FFT_M ? acc2[e].x : acc2[e - FFT_M].y; };
+  const double2* bsk_s = reinterpret_cast<const double2*>(bt_raw + L::OFF_BSK);
+  uint16_t* abar = reinterpret_cast<uint16_t*>(bt_raw + L::OFF_ABAR) + cl * BR_MAXN;
+  const uint32_t bar = tc::smem_u32(bt_raw + L::OFF_BAR);
+  volatile int* abort_s = reinterpret_cast<volatile int*>(bt_raw + L::OFF_BAR + 8);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bt_raw + L::OFF_BAR + 12);
+  const uint32_t bsk_dst = tc::smem_u32(bt_raw + L::OFF_BSK);
+
+  if (threadIdx.x == 0) {
+    tc::mbar_init(bar, 1);
+    tc::fence_mbar_init();
+    *abort_s = 0;
+  }
+  if (warp == 0) tc::tmem_alloc(tc::smem_u32(tmem_holder), L::TMEM_COLS);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (threadIdx.x == 0) br_stage_ggsw(bsk_dst, fbsk, bar);
+  const uint32_t tq = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
+                      ((uint32_t)(32 * cl) << 16);
+  const uint32_t t_fwd = tq, t_inv = tq + 128u;
+  const uint32_t t_own = tq + 256u + 128u * (uint32_t)p, t_oth = tq + 256u + 128u * (uint32_t)(p ^ 1);
+  if (p == 0) {  // one warp per lane quarter writes its twiddles
+#pragma unroll 1
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16], u[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        d2_to_words(tb.wf[(4 * g + q) * 32 + lane], t + 4 * q);
+        d2_to_words(tb.wf[lane * 32 + 4 * g + q], u + 4 * q);
+      }
+      tc::tmem_st_32x32_x16(t_fwd + 16u * g, t);
+      tc::tmem_st_32x32_x16(t_inv + 16u * g, u);
+    }
+    tc::tmem_st_wait();
+  }
+
+  const uint64_t* in = small_ct + (size_t)(valid ? ct : 0) * (n + 1);
+  const uint64_t* tv = tv_of(sel, valid ? ct : 0);
+  const int t64 = lane + 32 * p;
+  for (int i = t64; i < n; i += 64) abar[i] = valid ? (uint16_t)modswitch(in[i], LG) : 0;
+  const int bt = valid ? modswitch(in[n], LG) : 0;
+  const int r0 = (2 * FFT_N - bt) & (2 * FFT_N - 1);
+  for (int t = lane; t < FFT_M; t += 32) {
+    auto top = [&](int e) { return (uint32_t)((rot_coef(tv, e, r0) + 0x80000000ull) >> 32); };
+    acc2[t] = (p == 0) ? make_uint2(0u, 0u) : make_uint2(top(t), top(t + FFT_M));
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+
+  const int shift = 32 - base_log;
+  const uint32_t rnd = 1u << (shift - 1);
+  const double2* f_own = bsk_s + (size_t)(p * 2 + p) * FFT_M;
+  const double2* f_oth = bsk_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
+
+  for (int i = 0; i < n; ++i) {
+    const int a = abar[i];
+    const int ar = a & (FFT_N - 1);
+    const uint32_t flip0 = (a >= FFT_N) ? 0xffffffffu : 0u;
+    double2 x[FFT_R];
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      if ((m & 7) == 0) asm volatile("" ::: "memory");
+      const int j = lane + 32 * m;
+      const int t = j - ar;
+      const uint2 g = acc2[t & (FFT_M - 1)], own = acc2[j];
+      const bool sw = (unsigned)(t + FFT_M) < (unsigned)FFT_M;
+      const uint32_t w0 = (t < 0) ? ~flip0 : flip0, w1 = (t < -FFT_M) ? ~flip0 : flip0;
+      const uint32_t g0 = sw ? g.y : g.x, g1 = sw ? g.x : g.y;
+      const uint32_t v0 = ((g0 ^ w0) - w0) - own.x;
+      const uint32_t v1 = ((g1 ^ w1) - w1) - own.y;
+      const int d0 = (int)(v0 + rnd) >> shift;
+      const int d1 = (int)(v1 + rnd) >> shift;
+      x[m] = make_double2((double)d0, (double)d1);
+    }
+    // forward transform, the mid twiddles from tensor memory
+    crt_dft32<32, PNB_BR_CBANK>(x);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16];
+      tc::tmem_ld_32x32_x16(t_fwd + 16u * g, t);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) x[4 * g + q] = cmul(x[4 * g + q], words_to_d2(t + 4 * q));
+    }
+    warp_transpose_half(x, buf, lane);
+    crt_dft32<0, PNB_BR_CBANK>(x);
+    // this warp's spectrum to tensor memory for the other warp of the ciphertext
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) d2_to_words(x[4 * g + q], t + 4 * q);
+      tc::tmem_st_32x32_x16(t_own + 16u * g, t);
+    }
+    tc::tmem_st_wait();
+    // GGSW i must have landed in shared memory (bounded wait; parity = i mod 2).
+    if (!tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT)) {
+      *abort_s = 1;
+      atomicExch(&g_br_status, 1);
+    }
+    tc::tc_fence_before();
+    pair_sync(cl);
+    tc::tc_fence_after();
+    // output polynomial p = D_own * F[own row][p] + D_other * F[other row][p]
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16];
+      tc::tmem_ld_32x32_x16(t_oth + 16u * g, t);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int r = 4 * g + q;
+        const int e = r * 32 + lane;
+        const double2 fo = f_own[e], ft = f_oth[e];
+        const double2 dt = words_to_d2(t + 4 * q);
+        const double2 p0 = cmul(x[r], fo);
+        x[r] = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
+                            p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+      }
+    }
+    // Every warp is done with GGSW i and with the other warp's spectrum: stage GGSW i+1 while
+    // the inverse transforms run.
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    if (*abort_s) {  // uniform: read by every thread after the same barrier
+      if (threadIdx.x == 0) (void)tc::mbar_wait(bar, (uint32_t)(i & 1), BR_WAIT_LIMIT);
+      break;
+    }
+    if (threadIdx.x == 0 && i + 1 < n) {
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
+    }
+    // inverse transform, the conjugate twiddles from tensor memory
+    dit_dft32<PNB_BR_CBANK>(x);
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16];
+      tc::tmem_ld_32x32_x16(t_inv + 16u * g, t);
+      tc::tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 4; ++q) x[4 * g + q] = cmul_conj(x[4 * g + q], words_to_d2(t + 4 * q));
+    }
+    warp_transpose_half(x, buf, lane);
+    dit_dft32<PNB_BR_CBANK>(x);
+    untwist<10 + 32, PNB_BR_CBANK>(x);
+#pragma unroll
+    for (int m = 0; m < 32; ++m) {
+      if ((m & 7) == 0) asm volatile("" ::: "memory");
+      const int j = lane + 32 * m;
+      uint2 o = acc2[j];
+      o.x += scaled_f64_to_top32(x[m].x);
+      o.y += scaled_f64_to_top32(x[m].y);
+      acc2[j] = o;
+    }
+    __syncwarp();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(tmem_holder), L::TMEM_COLS);
+  }
+  // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
+  if (valid && !*abort_s) {
+    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    if (p == 0) {
+      for (int t = lane; t < FFT_N; t += 32) {
+        const uint64_t v = (uint64_t)acc_at(t == 0 ? 0 : FFT_N - t) << 32;
+        o[t] = (t == 0) ? v : (uint64_t)0 - v;
+      }
+    } else if (lane == 0) {
+      o[FFT_N] = (uint64_t)acc_at(0) << 32;
+    }
+  }
+}
+
+// Which single-level rotation runs: 1 = twiddles and exchange in tensor memory, 0 = in shared
+// memory.
+#ifndef PNB_BR_TMEM
+#define PNB_BR_TMEM 1
+#endif
+
+// ------------------------------------------------------------------------------------------
 // Blocked multi-level blind rotation (pbs_level 2..6).  A block bootstraps MLB_CPB ciphertexts
 // in lockstep, warp (2c + p) owning accumulator polynomial p of ciphertext c, like the single-
 // level kernel; per CMux it walks the gadget levels, and each level's part of the GGSW (the mask
@@ -777,13 +1016,22 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
       set_error("blind rotation: pbs_level %d not compiled", K->p.pbs_level);
       return PNB_ERR_UNSUPPORTED;
   }
+  const int blocks = (count + BR_CPB - 1) / BR_CPB;
+#if PNB_BR_TMEM
+  constexpr int smem = BrTmLayout<BR_CPB>::BYTES;
+  PNB_CUDA(cudaFuncSetAttribute(blind_rotate_tm_kernel<BR_CPB>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  blind_rotate_tm_kernel<BR_CPB><<<blocks, 64 * BR_CPB, smem, st>>>(
+      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+  PNB_CHECK_LAUNCH("blind_rotate_tm_kernel");
+#else
   constexpr int smem = BrLayout<BR_CPB>::BYTES;
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_kernel<BR_CPB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-  const int blocks = (count + BR_CPB - 1) / BR_CPB;
   blind_rotate_kernel<BR_CPB><<<blocks, 64 * BR_CPB, smem, st>>>(
       small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
   PNB_CHECK_LAUNCH("blind_rotate_kernel");
+#endif
   return PNB_OK;
 }
 
