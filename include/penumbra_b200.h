@@ -183,6 +183,19 @@ int pnb_lwe_contract_gather(const int8_t* W_dev, const int64_t* bias_dev, uint64
                             int K, const uint64_t* X_dev, const int32_t* index_dev, int groups,
                             uint64_t* Y_dev, int lwe_len, void* stream);
 
+/* The two contractions over ciphertext rows at explicit pitches: row r of X starts at word
+ * r * ldx, row r of Y at r * ldy (ldx, ldy >= lwe_len).  An even ldx with a 16-byte aligned X
+ * (2050 words for N = 2048, the layout the graph evaluator keeps) lets the operand move as TMA
+ * tiles (dense) or 16-byte copies (gathered); an odd pitch takes 8-byte copies.  Replaces the
+ * same reference loops as pnb_lwe_contract / pnb_lwe_contract_gather. */
+int pnb_lwe_contract_ld(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M,
+                        int K, const uint64_t* X_dev, int ldx, uint64_t* Y_dev, int ldy,
+                        int batch, int lwe_len, void* stream);
+int pnb_lwe_contract_gather_ld(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta,
+                               int M, int K, const uint64_t* X_dev, int ldx,
+                               const int32_t* index_dev, int groups, uint64_t* Y_dev, int ldy,
+                               int lwe_len, void* stream);
+
 /* Negacyclic products out[c] = a[c] * b[c] mod (X^N + 1) through the same f64 FFT the blind
  * rotation uses (a: small signed integers, |a| < 2^31; b: u64 torus), count polynomials.
  * Diagnostic entry point for the FFT's precision; no reference counterpart. */

@@ -23,7 +23,7 @@ __all__ = [
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
     "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys", "radix_merge",
     "TensorDesc", "KeyRing", "op_plan", "requant_batch", "argmax_batch", "add_batch",
-    "radix_plan",
+    "radix_plan", "lwe_contract_ld", "lwe_contract_gather_ld",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -90,6 +90,12 @@ _SIGS = {
                                           C.c_void_p]),
     "pnb_lwe_contract": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
                                    C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "pnb_lwe_contract_ld": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int, C.c_int,
+                                      C.c_void_p, C.c_int, C.c_void_p, C.c_int, C.c_int, C.c_int,
+                                      C.c_void_p]),
+    "pnb_lwe_contract_gather_ld": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int,
+                                             C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
+                                             C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
     "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_int, C.c_void_p]),
     "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
@@ -464,6 +470,52 @@ def lwe_contract_gather(W: torch.Tensor, bias: torch.Tensor | None, delta: int,
                                              _ptr(_u64(X).contiguous()),
                                              _ptr(index.contiguous()), G, _ptr(out), L,
                                              _stream(X.device)))
+    return out
+
+
+def lwe_contract_ld(W: torch.Tensor, bias: torch.Tensor | None, delta: int, X: torch.Tensor,
+                    lwe_len: int, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``lwe_contract`` over rows at a pitch: X [B, K, ldx] holds ``lwe_len`` words per row
+    (ldx >= lwe_len); the result is [B, M, ldx] at the same pitch (words past ``lwe_len`` are
+    left as they were)."""
+    if W.dtype != torch.int8:
+        raise TypeError("W must be int8")
+    M, K = W.shape
+    B, K2, ld = X.shape
+    if K2 != K:
+        raise ValueError(f"X has {K2} inputs, W expects {K}")
+    if out is None:
+        out = torch.zeros((B, M, ld), dtype=torch.int64, device=X.device)
+    bias_t = None if bias is None else bias.to(device=X.device, dtype=torch.int64).contiguous()
+    with torch.cuda.device(X.device):
+        _check("pnb_lwe_contract_ld",
+               lib().pnb_lwe_contract_ld(_ptr(W.contiguous()), _ptr(bias_t), delta % (1 << 64),
+                                         M, K, _ptr(_u64(X).contiguous()), ld, _ptr(out),
+                                         out.shape[-1], B, lwe_len, _stream(X.device)))
+    return out
+
+
+def lwe_contract_gather_ld(W: torch.Tensor, bias: torch.Tensor | None, delta: int,
+                           X: torch.Tensor, index: torch.Tensor, lwe_len: int,
+                           out: torch.Tensor | None = None) -> torch.Tensor:
+    """``lwe_contract_gather`` over rows at a pitch (X [*, ldx]; result [G, M, ldx])."""
+    if W.dtype != torch.int8 or index.dtype != torch.int32:
+        raise TypeError("W must be int8 and index int32")
+    M, K = W.shape
+    G, K2 = index.shape
+    if K2 != K:
+        raise ValueError(f"index has {K2} taps, W expects {K}")
+    ld = X.shape[-1]
+    if out is None:
+        out = torch.zeros((G, M, ld), dtype=torch.int64, device=X.device)
+    bias_t = None if bias is None else bias.to(device=X.device, dtype=torch.int64).contiguous()
+    with torch.cuda.device(X.device):
+        _check("pnb_lwe_contract_gather_ld",
+               lib().pnb_lwe_contract_gather_ld(_ptr(W.contiguous()), _ptr(bias_t),
+                                                delta % (1 << 64), M, K,
+                                                _ptr(_u64(X).contiguous()), ld,
+                                                _ptr(index.contiguous()), G, _ptr(out),
+                                                out.shape[-1], lwe_len, _stream(X.device)))
     return out
 
 

@@ -416,6 +416,37 @@ int pnb_lwe_contract_gather(const int8_t* W_dev, const int64_t* bias_dev, uint64
                              lwe_len, (cudaStream_t)stream);
 }
 
+int pnb_lwe_contract_ld(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta, int M,
+                        int K, const uint64_t* X_dev, int ldx, uint64_t* Y_dev, int ldy,
+                        int batch, int lwe_len, void* stream) {
+  if (batch > 0 && (!W_dev || !X_dev || !Y_dev)) {
+    set_error("contract: NULL buffer");
+    return PNB_ERR_INVALID;
+  }
+  if (ldx <= 0 || ldy <= 0) {
+    set_error("contract: row pitches must be positive (got %d, %d)", ldx, ldy);
+    return PNB_ERR_INVALID;
+  }
+  return lwe_contract_tc(W_dev, bias_dev, delta, M, K, X_dev, Y_dev, batch, lwe_len,
+                         (cudaStream_t)stream, ldx, ldy);
+}
+
+int pnb_lwe_contract_gather_ld(const int8_t* W_dev, const int64_t* bias_dev, uint64_t delta,
+                               int M, int K, const uint64_t* X_dev, int ldx,
+                               const int32_t* index_dev, int groups, uint64_t* Y_dev, int ldy,
+                               int lwe_len, void* stream) {
+  if (groups > 0 && (!W_dev || !X_dev || !index_dev || !Y_dev)) {
+    set_error("contract_gather: NULL buffer");
+    return PNB_ERR_INVALID;
+  }
+  if (ldx <= 0 || ldy <= 0) {
+    set_error("contract_gather: row pitches must be positive (got %d, %d)", ldx, ldy);
+    return PNB_ERR_INVALID;
+  }
+  return lwe_contract_gather_placed(W_dev, bias_dev, delta, M, K, X_dev, index_dev, groups,
+                                    Y_dev, lwe_len, 0, (cudaStream_t)stream, ldx, ldy);
+}
+
 int pnb_fft_negacyclic_mul(int device, int N, const int64_t* a_dev, const uint64_t* b_dev,
                            uint64_t* out_dev, int count, void* stream) {
   if (count < 0 || (count > 0 && (!a_dev || !b_dev || !out_dev))) {

@@ -3,8 +3,10 @@
 //
 // Replaces the reference's per-sample node walk (runtime/src/eval.rs:86-166): the program built
 // by plan.cpp runs once per chunk of samples, every instruction over the whole chunk.  Buffers
-// are [sample][element][kN+1] u64 big-key LWE ciphertexts; the per-element tables (weights,
-// gather indices, linear-combination coefficients, test-vector choices) are uploaded once.
+// are [sample][element][pitch] u64 big-key LWE ciphertexts of kN+1 words, the pitch rounded up to
+// an even number of words so that every row starts 16-byte aligned (the contraction then reads
+// its operand by TMA tiles or 16-byte copies); the per-element tables (weights, gather indices,
+// linear-combination coefficients, test-vector choices) are uploaded once.
 #include <algorithm>
 #include <cmath>
 #include <cstring>
@@ -42,6 +44,7 @@ struct LinArgs {
   uint64_t* dst;
   int64_t E, rows;  // elements per sample, rows = batch * E
   int L, nt;
+  int ld;           // row pitch (words) of dst and every source
   const uint64_t* src[LIN_TERMS];
   int64_t srcE[LIN_TERMS];
   const int64_t* coef[LIN_TERMS];
@@ -65,19 +68,33 @@ __global__ void __launch_bounds__(256) lin_kernel(LinArgs a) {
     if (t < a.nt) {
       const int64_t m = a.map[t] ? a.map[t][e] : e;
       if (m >= 0) {
-        s[t] = a.src[t] + ((size_t)b * a.srcE[t] + m) * a.L;
+        s[t] = a.src[t] + ((size_t)b * a.srcE[t] + m) * a.ld;
         k[t] = (uint64_t)(a.coef[t] ? a.coef[t][e] : a.coef_u[t]);
       }
     }
   }
   const uint64_t body = a.cst ? a.cst[e] : a.cst_u;
-  uint64_t* d = a.dst + (size_t)row * a.L;
+  uint64_t* d = a.dst + (size_t)row * a.ld;
   for (int c = threadIdx.x & 127; c < a.L; c += 128) {
     uint64_t v = (c == a.L - 1) ? body : 0;
 #pragma unroll
     for (int t = 0; t < LIN_TERMS; ++t)
       if (s[t]) v += k[t] * s[t][c];
     d[c] = v;
+  }
+}
+
+// Copy `rows` rows of L words per sample between row pitches: dst row (b, e) at
+// (b * dst_rows + e) * dst_ld, src row at (b * src_rows + src_off + e) * src_ld.
+__global__ void repitch_kernel(uint64_t* __restrict__ dst, int64_t dst_rows, int dst_ld,
+                               const uint64_t* __restrict__ src, int64_t src_rows,
+                               int64_t src_off, int src_ld, int64_t rows, int batch, int L) {
+  const int64_t n = (int64_t)batch * rows;
+  for (int64_t r = blockIdx.x; r < n; r += gridDim.x) {
+    const int64_t b = r / rows, e = r - b * rows;
+    const uint64_t* sp = src + ((size_t)b * src_rows + src_off + e) * src_ld;
+    uint64_t* dp = dst + ((size_t)b * dst_rows + e) * dst_ld;
+    for (int c = threadIdx.x; c < L; c += blockDim.x) dp[c] = sp[c];
   }
 }
 
@@ -168,14 +185,16 @@ void free_chunk(pnb_evaluator* ev) {
 }
 
 int64_t row_words(const pnb_params& p) { return (int64_t)p.k * p.N + 1; }
+// Internal row pitch: kN+1 rounded up to an even number of words (16-byte aligned rows).
+int64_t row_pitch(const pnb_params& p) { return (row_words(p) + 1) & ~(int64_t)1; }
 
 int alloc_chunk(pnb_evaluator* ev, int chunk) {
   free_chunk(ev);
-  const int64_t L = row_words(ev->params);
+  const int64_t LP = row_pitch(ev->params);
   const auto& P = ev->prog;
   ev->bufs.assign(P.bufs.size(), nullptr);
   for (size_t i = 0; i < P.bufs.size(); ++i)
-    PNB_CUDA(cudaMalloc((void**)&ev->bufs[i], (size_t)chunk * P.bufs[i].elems * L * 8));
+    PNB_CUDA(cudaMalloc((void**)&ev->bufs[i], (size_t)chunk * P.bufs[i].elems * LP * 8));
   ev->gathers.assign(P.code.size(), nullptr);
   int64_t max_rows = 0;
   for (size_t i = 0; i < P.code.size(); ++i) {
@@ -212,6 +231,7 @@ int run_lin(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
   a.E = P.bufs[I.dst].elems;
   a.rows = (int64_t)batch * a.E;
   a.L = (int)row_words(ev->params);
+  a.ld = (int)row_pitch(ev->params);
   a.nt = (int)I.terms.size();
   if (a.nt > LIN_TERMS) {
     set_error("internal: linear combination with %d terms", a.nt);
@@ -239,6 +259,7 @@ int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
   const int64_t E = P.bufs[I.dst].elems;
   const int64_t rows = (int64_t)batch * E;
   const int L = (int)row_words(ev->params);
+  const int LP = (int)row_pitch(ev->params);
   // stage the bootstrap input 2^shift * src + offset in the destination buffer
   LinArgs a;
   memset(&a, 0, sizeof a);
@@ -246,6 +267,7 @@ int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
   a.E = E;
   a.rows = rows;
   a.L = L;
+  a.ld = LP;
   a.nt = 1;
   a.src[0] = ev->bufs[I.src];
   a.srcE[0] = P.bufs[I.src].elems;
@@ -257,11 +279,11 @@ int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
   const pnb_keys* K = ev->keys[I.level];
   for (int64_t r0 = 0; r0 < rows; r0 += ev->max_pbs_rows) {
     const int cnt = (int)std::min<int64_t>(ev->max_pbs_rows, rows - r0);
-    uint64_t* x = ev->bufs[I.dst] + (size_t)r0 * L;
-    int rc = keyswitch_launch(ev->client, x, ev->small, cnt, ev->ks_ws, st);
+    uint64_t* x = ev->bufs[I.dst] + (size_t)r0 * LP;
+    int rc = keyswitch_launch(ev->client, x, ev->small, cnt, ev->ks_ws, st, LP);
     if (rc) return rc;
     // row r of the slice is element (r0 + r) % E of its sample
-    rc = blind_rotate_sel(K, ev->tvs, D.tv, (int)E, (int)(r0 % E), ev->small, x, cnt, st);
+    rc = blind_rotate_sel(K, ev->tvs, D.tv, (int)E, (int)(r0 % E), ev->small, x, cnt, st, LP);
     if (rc) return rc;
   }
   return PNB_OK;
@@ -270,11 +292,13 @@ int run_pbs(pnb_evaluator* ev, const plan::Instr& I, const DevInstr& D, int batc
 int run_contract(pnb_evaluator* ev, size_t i, const plan::Instr& I, const DevInstr& D,
                  int batch, cudaStream_t st) {
   const int L = (int)row_words(ev->params);
+  const int LP = (int)row_pitch(ev->params);
   if (I.gather.empty())
     return lwe_contract_tc(D.W, D.bias, I.bias_delta, I.M, I.K, ev->bufs[I.src],
-                           ev->bufs[I.dst], batch, L, st);
+                           ev->bufs[I.dst], batch, L, st, LP, LP);
   return lwe_contract_gather_placed(D.W, D.bias, I.bias_delta, I.M, I.K, ev->bufs[I.src],
-                                    ev->gathers[i], batch * I.P, ev->bufs[I.dst], L, I.P, st);
+                                    ev->gathers[i], batch * I.P, ev->bufs[I.dst], L, I.P, st,
+                                    LP, LP);
 }
 
 }  // namespace
@@ -707,7 +731,7 @@ int evaluator_finish(pnb_evaluator* ev, const pnb_plan* p, size_t max_bytes) {
   if (rc == PNB_OK) {
     // chunk size: as many samples as fit the memory budget
     int64_t per_sample = 0;
-    for (const auto& b : P.bufs) per_sample += b.elems * row_words(p->params) * 8;
+    for (const auto& b : P.bufs) per_sample += b.elems * row_pitch(p->params) * 8;
     size_t budget = max_bytes;
     if (budget == 0) {
       size_t fr = 0, tot = 0;
@@ -765,12 +789,14 @@ int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t*
   const int chunk = ev->chunk;
   for (int b0 = 0; b0 < batch && rc == PNB_OK; b0 += chunk) {
     const int nb = std::min(chunk, batch - b0);
+    const int LP = (int)row_pitch(ev->params);
+    auto grid_of = [](int64_t rows) { return (unsigned)std::min<int64_t>(rows, 148 * 32); };
     int64_t off = 0;
     for (const auto& io : P.inputs) {
-      cudaError_t e = cudaMemcpy2DAsync(
-          ev->bufs[io.buf], (size_t)io.elems * L * 8,
-          in_dev + ((size_t)b0 * P.input_elems + off) * L, (size_t)P.input_elems * L * 8,
-          (size_t)io.elems * L * 8, nb, cudaMemcpyDeviceToDevice, st);
+      repitch_kernel<<<grid_of((int64_t)nb * io.elems), 256, 0, st>>>(
+          ev->bufs[io.buf], io.elems, LP, in_dev + (size_t)b0 * P.input_elems * L,
+          P.input_elems, off, (int)L, io.elems, nb, (int)L);
+      cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_status(e, "pnb_evaluate: input copy");
       off += io.elems;
     }
@@ -785,10 +811,11 @@ int pnb_evaluate(pnb_evaluator* ev, const uint64_t* in_dev, int batch, uint64_t*
     off = 0;
     for (const auto& io : P.outputs) {
       if (rc) break;
-      cudaError_t e = cudaMemcpy2DAsync(
-          out_dev + ((size_t)b0 * P.output_elems + off) * L, (size_t)P.output_elems * L * 8,
-          ev->bufs[io.buf], (size_t)io.elems * L * 8, (size_t)io.elems * L * 8, nb,
-          cudaMemcpyDeviceToDevice, st);
+      // output tensor io is columns [off, off + elems) of each sample's output rows
+      repitch_kernel<<<grid_of((int64_t)nb * io.elems), 256, 0, st>>>(
+          out_dev + ((size_t)b0 * P.output_elems + off) * L, P.output_elems, (int)L,
+          ev->bufs[io.buf], io.elems, 0, LP, io.elems, nb, (int)L);
+      cudaError_t e = cudaGetLastError();
       if (e != cudaSuccess) return cuda_status(e, "pnb_evaluate: output copy");
       off += io.elems;
     }

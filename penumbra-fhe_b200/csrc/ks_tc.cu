@@ -80,13 +80,13 @@ int make_tmap_u8_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t
 // ------------------------------------------------------------------------------------------
 // Digits: D[c][i*L + j] = signed digit j (most significant first) of in[c][i].
 // ------------------------------------------------------------------------------------------
-__global__ void ks_digits_kernel(const uint64_t* __restrict__ in, int count, int big,
+__global__ void ks_digits_kernel(const uint64_t* __restrict__ in, int count, int big, int ld,
                                  int base_log, int level, int8_t* __restrict__ D) {
   const size_t idx = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (size_t)count * big) return;
   const size_t c = idx / big;
   const int i = (int)(idx % big);
-  const uint64_t a = in[c * (big + 1) + i];
+  const uint64_t a = in[c * ld + i];
   const int total = base_log * level;
   uint64_t st = (a >> (64 - total)) + ((a >> (63 - total)) & 1u);
   const uint64_t mask = (1ull << base_log) - 1, half = 1ull << (base_log - 1);
@@ -119,7 +119,7 @@ __global__ void __launch_bounds__(192, 1) ks_gemm_kernel(const __grid_constant__
                                                          const __grid_constant__ CUtensorMap tmB,
                                                          const uint64_t* __restrict__ in,
                                                          uint64_t* __restrict__ out, int count,
-                                                         int n, int big, int k_blocks) {
+                                                         int n, int big, int ld, int k_blocks) {
   extern __shared__ unsigned char ks_raw[];
   const uint32_t raw = tc::smem_u32(ks_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -201,7 +201,7 @@ __global__ void __launch_bounds__(192, 1) ks_gemm_kernel(const __grid_constant__
     if (tc::mbar_wait(accum, 0, KS_WAIT_LIMIT)) {
       tc::tc_fence_after();
       const int col0 = nb0 / 8;
-      const uint64_t body = (row < count) ? in[(size_t)row * (big + 1) + big] : 0;
+      const uint64_t body = (row < count) ? in[(size_t)row * ld + big] : 0;
 #pragma unroll 1
       for (int chunk = 0; chunk < KS_BN / 32; ++chunk) {
         uint32_t r[32];
@@ -232,12 +232,17 @@ size_t ks_tc_workspace_bytes(const pnb_params& p, int count) {
   return (d + 255) & ~(size_t)255;
 }
 
-// in: [count][kN+1] big-key ciphertexts; out: [count][n+1]; digits: scratch of
-// ks_tc_workspace_bytes.
+// in: [count][in_ld] big-key ciphertexts (kN+1 words used; in_ld 0 = kN+1); out: [count][n+1];
+// digits: scratch of ks_tc_workspace_bytes.
 int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count, void* digits,
-                 cudaStream_t st) {
+                 cudaStream_t st, int in_ld) {
   const pnb_params& p = K->p;
   const int big = p.k * p.N;
+  const int ld = in_ld > 0 ? in_ld : big + 1;
+  if (ld < big + 1) {
+    set_error("keyswitch: row pitch %d is shorter than a %d-word ciphertext", ld, big + 1);
+    return PNB_ERR_INVALID;
+  }
   const int kdim = big * p.ks_level;
   if (kdim % KS_BK != 0 || p.ks_base_log > 7 || p.ks_base_log < 1 ||
       p.ks_base_log * p.ks_level >= 64) {
@@ -251,8 +256,8 @@ int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count
   }
   int8_t* D = static_cast<int8_t*>(digits);
   const size_t tot = (size_t)count * big;
-  ks_digits_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(in, count, big, p.ks_base_log,
-                                                                 p.ks_level, D);
+  ks_digits_kernel<<<(unsigned)((tot + 255) / 256), 256, 0, st>>>(in, count, big, ld,
+                                                                 p.ks_base_log, p.ks_level, D);
   PNB_CHECK_LAUNCH("ks_digits_kernel");
   CUtensorMap tmA, tmB;
   int rc = make_tmap_u8_2d(&tmA, D, (uint64_t)kdim, (uint64_t)count, (uint64_t)kdim, KS_BK,
@@ -276,7 +281,7 @@ int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count
     return PNB_ERR_INVALID;
   }
   dim3 grid(n_tiles, m_tiles);
-  ks_gemm_kernel<<<grid, 192, KS_SMEM, st>>>(tmA, tmB, in, out, count, p.n, big,
+  ks_gemm_kernel<<<grid, 192, KS_SMEM, st>>>(tmA, tmB, in, out, count, p.n, big, ld,
                                              kdim / KS_BK);
   PNB_CHECK_LAUNCH("ks_gemm_kernel");
   return PNB_OK;

@@ -157,7 +157,7 @@ int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaSt
 // Keyswitch (tensor cores, ks_tc.cu): digit scratch from `digits` or the stream allocator.
 // ------------------------------------------------------------------------------------------
 int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,
-                     void* digits, cudaStream_t st) {
+                     void* digits, cudaStream_t st, int in_ld) {
   if (count <= 0) return PNB_OK;
   void* d = digits;
   bool own = false;
@@ -166,7 +166,7 @@ int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int c
     if (e != cudaSuccess) return cuda_status(e, "cudaMallocAsync(keyswitch digits)");
     own = true;
   }
-  int rc = keyswitch_tc(K, in, out, count, d, st);
+  int rc = keyswitch_tc(K, in, out, count, d, st, in_ld);
   if (own) {
     cudaError_t e = cudaFreeAsync(d, st);
     if (rc == PNB_OK && e != cudaSuccess) rc = cuda_status(e, "cudaFreeAsync(keyswitch digits)");
@@ -247,7 +247,7 @@ __device__ __forceinline__ void br_stage_ggsw(uint32_t dst, const double2* src, 
 template <int CPB>
 __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel,
-    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
+    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int out_ld, int count, int n,
     int base_log, FftTables tb) {
   using L = BrLayout<CPB>;
   extern __shared__ __align__(128) unsigned char br_raw[];
@@ -370,7 +370,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_kernel(
   }
   // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
   if (valid && !*abort_s) {
-    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    uint64_t* o = out + (size_t)ct * out_ld;
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32) {
         const uint64_t v = (uint64_t)acc_at(t == 0 ? 0 : FFT_N - t) << 32;
@@ -423,10 +423,23 @@ __device__ __forceinline__ double2 words_to_d2(const uint32_t* t) {
                       __hiloint2double((int)t[3], (int)t[2]));
 }
 
+// Complex values per tensor-memory round trip in the rotation (4: 16 columns, 8: 32 columns);
+// tcgen05.wait::ld waits for every load in flight, so a round trip is one load and one wait.
+#ifndef PNB_BR_TM_CHUNK
+#define PNB_BR_TM_CHUNK 8
+#endif
+template <int C>
+__device__ __forceinline__ void tm_load(uint32_t taddr, uint32_t (&t)[4 * C]) {
+  static_assert(C == 4 || C == 8, "4 or 8 complex values per load");
+  if constexpr (C == 4) tc::tmem_ld_32x32_x16(taddr, t);
+  else tc::tmem_ld_32x32_nowait(taddr, t);
+  tc::tmem_ld_wait();
+}
+
 template <int CPB>
 __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel,
-    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int count, int n,
+    const double2* __restrict__ fbsk, uint64_t* __restrict__ out, int out_ld, int count, int n,
     int base_log, FftTables tb) {
   static_assert(CPB == 4, "the lane-quarter mapping needs four ciphertexts per block");
   using L = BrTmLayout<CPB>;
@@ -516,13 +529,13 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
     }
     // forward transform, the mid twiddles from tensor memory
     crt_dft32<32, PNB_BR_CBANK>(x);
+    constexpr int TC = PNB_BR_TM_CHUNK;
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      uint32_t t[16];
-      tc::tmem_ld_32x32_x16(t_fwd + 16u * g, t);
-      tc::tmem_ld_wait();
+    for (int g = 0; g < 32 / TC; ++g) {
+      uint32_t t[4 * TC];
+      tm_load<TC>(t_fwd + 4u * TC * g, t);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) x[4 * g + q] = cmul(x[4 * g + q], words_to_d2(t + 4 * q));
+      for (int q = 0; q < TC; ++q) x[TC * g + q] = cmul(x[TC * g + q], words_to_d2(t + 4 * q));
     }
     warp_transpose_half(x, buf, lane);
     crt_dft32<0, PNB_BR_CBANK>(x);
@@ -545,13 +558,12 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
     tc::tc_fence_after();
     // output polynomial p = D_own * F[own row][p] + D_other * F[other row][p]
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      uint32_t t[16];
-      tc::tmem_ld_32x32_x16(t_oth + 16u * g, t);
-      tc::tmem_ld_wait();
+    for (int g = 0; g < 32 / TC; ++g) {
+      uint32_t t[4 * TC];
+      tm_load<TC>(t_oth + 4u * TC * g, t);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int r = 4 * g + q;
+      for (int q = 0; q < TC; ++q) {
+        const int r = TC * g + q;
         const int e = r * 32 + lane;
         const double2 fo = f_own[e], ft = f_oth[e];
         const double2 dt = words_to_d2(t + 4 * q);
@@ -576,12 +588,12 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
     // inverse transform, the conjugate twiddles from tensor memory
     dit_dft32<PNB_BR_CBANK>(x);
 #pragma unroll
-    for (int g = 0; g < 8; ++g) {
-      uint32_t t[16];
-      tc::tmem_ld_32x32_x16(t_inv + 16u * g, t);
-      tc::tmem_ld_wait();
+    for (int g = 0; g < 32 / TC; ++g) {
+      uint32_t t[4 * TC];
+      tm_load<TC>(t_inv + 4u * TC * g, t);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) x[4 * g + q] = cmul_conj(x[4 * g + q], words_to_d2(t + 4 * q));
+      for (int q = 0; q < TC; ++q)
+        x[TC * g + q] = cmul_conj(x[TC * g + q], words_to_d2(t + 4 * q));
     }
     warp_transpose_half(x, buf, lane);
     dit_dft32<PNB_BR_CBANK>(x);
@@ -605,7 +617,7 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
   }
   // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
   if (valid && !*abort_s) {
-    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    uint64_t* o = out + (size_t)ct * out_ld;
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32) {
         const uint64_t v = (uint64_t)acc_at(t == 0 ? 0 : FFT_N - t) << 32;
@@ -688,7 +700,7 @@ __device__ __forceinline__ void mlb_stage(uint32_t dst, const double2* fbsk, int
 template <int L, int BETA>
 __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
     const uint64_t* __restrict__ small_ct, TvSel sel, const double2* __restrict__ fbsk,
-    uint64_t* __restrict__ out, int count, int n, int base_log, FftTables tb) {
+    uint64_t* __restrict__ out, int out_ld, int count, int n, int base_log, FftTables tb) {
   using Y = MlbLayout;
   extern __shared__ __align__(128) unsigned char mlb_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -939,7 +951,7 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   }
   // Sample extraction of coefficient 0 into an LWE of dimension N under the big key.
   if (valid && !aborted) {
-    uint64_t* o = out + (size_t)ct * (FFT_N + 1);
+    uint64_t* o = out + (size_t)ct * out_ld;
     if (p == 0) {
       for (int t = lane; t < FFT_N; t += 32)
         o[t] = (t == 0) ? acc_at(0) : (uint64_t)0 - acc_at(FFT_N - t);
@@ -951,13 +963,13 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
 
 template <int L, int BETA>
 static int launch_mlb(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64_t* out,
-                      int count, FftTables tb, cudaStream_t st) {
+                      int out_ld, int count, FftTables tb, cudaStream_t st) {
   constexpr int smem = MlbLayout::BYTES;
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_mlb_kernel<L, BETA>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   const int blocks = (count + MLB_CPB - 1) / MLB_CPB;
   blind_rotate_mlb_kernel<L, BETA><<<blocks, 64 * MLB_CPB, smem, st>>>(
-      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+      small, tv, K->fbsk, out, out_ld, count, K->p.n, K->p.pbs_base_log, tb);
   PNB_CHECK_LAUNCH("blind_rotate_mlb_kernel");
   return PNB_OK;
 }
@@ -965,10 +977,12 @@ static int launch_mlb(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64
 // The key sets the graph planner uses get kernels with compile-time gadget constants.
 template <int L, int B0, int B1 = 0>
 static int launch_ml_any(const pnb_keys* K, TvSel tv, const uint64_t* small, uint64_t* out,
-                         int count, FftTables tb, cudaStream_t st) {
-  if (B0 > 0 && K->p.pbs_base_log == B0) return launch_mlb<L, B0>(K, tv, small, out, count, tb, st);
-  if (B1 > 0 && K->p.pbs_base_log == B1) return launch_mlb<L, B1>(K, tv, small, out, count, tb, st);
-  return launch_mlb<L, 0>(K, tv, small, out, count, tb, st);
+                         int out_ld, int count, FftTables tb, cudaStream_t st) {
+  if (B0 > 0 && K->p.pbs_base_log == B0)
+    return launch_mlb<L, B0>(K, tv, small, out, out_ld, count, tb, st);
+  if (B1 > 0 && K->p.pbs_base_log == B1)
+    return launch_mlb<L, B1>(K, tv, small, out, out_ld, count, tb, st);
+  return launch_mlb<L, 0>(K, tv, small, out, out_ld, count, tb, st);
 }
 
 static bool br_supported(const pnb_params& p) {
@@ -987,7 +1001,8 @@ int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* s
 }
 
 int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_idx, int period,
-                     int first, const uint64_t* small, uint64_t* out, int count, cudaStream_t st) {
+                     int first, const uint64_t* small, uint64_t* out, int count, cudaStream_t st,
+                     int out_ld) {
   if (tv_idx && (period <= 0 || first < 0)) {
     set_error("blind rotation: test-vector period must be positive");
     return PNB_ERR_INVALID;
@@ -1000,18 +1015,23 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
               K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
   }
+  if (out_ld == 0) out_ld = FFT_N + 1;
+  if (out_ld < FFT_N + 1) {
+    set_error("blind rotation: output row pitch %d is shorter than %d words", out_ld, FFT_N + 1);
+    return PNB_ERR_INVALID;
+  }
   if (count <= 0) return PNB_OK;
   FftTables tb;
   int rc = fft_tables_get(&tb);
   if (rc) return rc;
   switch (K->p.pbs_level) {
     case 1: break;
-    case 2: return launch_ml_any<2, 15>(K, tv, small, out, count, tb, st);
-    case 3: return launch_ml_any<3, 11>(K, tv, small, out, count, tb, st);
-    case 4: return launch_ml_any<4, 10>(K, tv, small, out, count, tb, st);
-    case 5: return launch_ml_any<5, 8>(K, tv, small, out, count, tb, st);
-    case 6: return launch_ml_any<6, 7>(K, tv, small, out, count, tb, st);
-    case 9: return launch_mlb<9, 5>(K, tv, small, out, count, tb, st);
+    case 2: return launch_ml_any<2, 15>(K, tv, small, out, out_ld, count, tb, st);
+    case 3: return launch_ml_any<3, 11>(K, tv, small, out, out_ld, count, tb, st);
+    case 4: return launch_ml_any<4, 10>(K, tv, small, out, out_ld, count, tb, st);
+    case 5: return launch_ml_any<5, 8>(K, tv, small, out, out_ld, count, tb, st);
+    case 6: return launch_ml_any<6, 7>(K, tv, small, out, out_ld, count, tb, st);
+    case 9: return launch_mlb<9, 5>(K, tv, small, out, out_ld, count, tb, st);
     default:
       set_error("blind rotation: pbs_level %d not compiled", K->p.pbs_level);
       return PNB_ERR_UNSUPPORTED;
@@ -1022,14 +1042,14 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_tm_kernel<BR_CPB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   blind_rotate_tm_kernel<BR_CPB><<<blocks, 64 * BR_CPB, smem, st>>>(
-      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+      small, tv, K->fbsk, out, out_ld, count, K->p.n, K->p.pbs_base_log, tb);
   PNB_CHECK_LAUNCH("blind_rotate_tm_kernel");
 #else
   constexpr int smem = BrLayout<BR_CPB>::BYTES;
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate_kernel<BR_CPB>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   blind_rotate_kernel<BR_CPB><<<blocks, 64 * BR_CPB, smem, st>>>(
-      small, tv, K->fbsk, out, count, K->p.n, K->p.pbs_base_log, tb);
+      small, tv, K->fbsk, out, out_ld, count, K->p.n, K->p.pbs_base_log, tb);
   PNB_CHECK_LAUNCH("blind_rotate_kernel");
 #endif
   return PNB_OK;

@@ -24,11 +24,14 @@ struct pnb_keys {
 namespace pnb {
 int keygen_device(pnb_keys* K, cudaStream_t st);
 int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaStream_t st);
+// Row pitches in words (`*_ld`, 0 = contiguous rows of the natural length) let the graph
+// evaluator keep its ciphertext rows 16-byte aligned.
 int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,
-                     void* digits, cudaStream_t st);
+                     void* digits, cudaStream_t st, int in_ld = 0);
 // Per-ciphertext test vectors: ciphertext c starts from tvs + tv_idx[(first + c) % period] * N.
 int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_idx, int period,
-                     int first, const uint64_t* small, uint64_t* out, int count, cudaStream_t st);
+                     int first, const uint64_t* small, uint64_t* out, int count, cudaStream_t st,
+                     int out_ld = 0);
 int blind_rotate_launch(const pnb_keys* K, const uint64_t* tv, const uint64_t* small,
                         uint64_t* out, int count, cudaStream_t st);
 size_t pbs_workspace_bytes(const pnb_keys* K, int count);
@@ -49,17 +52,18 @@ int phase_lwe(const pnb_keys* K, const uint64_t* ct, uint64_t* phase, int count,
 int measure_fp64_peak(double* tflops);
 int wait_probe(uint32_t polls, int* warps_gave_up);
 int lwe_contract_tc(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
-                    const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st);
+                    const uint64_t* X, uint64_t* Y, int batch, int L, cudaStream_t st,
+                    int ldx = 0, int ldy = 0);
 // As lwe_contract_gather, with group g = b*P + p written to output row (b*M + m)*P + p
 // (the channel-major [sample][channel][position] layout of a convolution); P = 0: [g][m].
 int lwe_contract_gather_placed(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                                const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
-                               int P, cudaStream_t st);
+                               int P, cudaStream_t st, int ldx = 0, int ldy = 0);
 int lwe_contract_gather(const int8_t* W, const int64_t* bias, uint64_t delta, int M, int K,
                         const uint64_t* X, const int32_t* idx, int G, uint64_t* Y, int L,
                         cudaStream_t st);
 int keyswitch_tc(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count, void* digits,
-                 cudaStream_t st);
+                 cudaStream_t st, int in_ld = 0);
 size_t ks_tc_workspace_bytes(const pnb_params& p, int count);
 int tc_status_read_and_clear(int* out);
 bool fft_tables_ready();

@@ -88,3 +88,57 @@ def test_contract_gather_matches_im2col(pnb, oracle):
     want = oracle.contract(Wt, bias, delta, Xg)
     assert np.array_equal(got, want)
     assert pnb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("M,K,B,L,ld", [
+    (128, 784, 2, 2049, 2050),   # the evaluator's pitch: TMA tiles
+    (10, 36, 3, 2049, 2050),     # rows of one group end inside a stage: the next group's
+                                 # rows meet zero weights, the last group's read past the end
+    (200, 130, 5, 2049, 2052),   # two M tiles, a wider pitch
+    (33, 65, 2, 301, 302),       # ragged tiles
+    (16, 72, 3, 2049, 2049),     # odd pitch: 8-byte gathers
+])
+def test_contract_pitched_bit_exact(pnb, oracle, M, K, B, L, ld):
+    rng = np.random.default_rng(M * 7 + K + ld)
+    W = rng.integers(-128, 128, (M, K), dtype=np.int64)
+    X = rng.integers(0, 1 << 63, (B, K, ld), dtype=np.uint64) * np.uint64(2) + \
+        rng.integers(0, 2, (B, K, ld), dtype=np.uint64)
+    bias = rng.integers(-1000, 1000, M)
+    delta = 1 << 45
+    out = torch.full((B, M, ld), 7, dtype=torch.int64, device="cuda")
+    got = pnb.lwe_contract_ld(torch.tensor(W.astype(np.int8), device="cuda"),
+                              torch.tensor(bias, device="cuda"), delta,
+                              torch.tensor(X.view(np.int64), device="cuda"), L, out=out)
+    got = got.cpu().numpy().view(np.uint64)
+    want = oracle.contract(W, bias, delta, np.ascontiguousarray(X[:, :, :L]))
+    assert np.array_equal(got[:, :, :L], want)
+    assert np.all(got[:, :, L:] == 7)  # the pad words are left alone
+    assert pnb.device_status(0) == 0
+
+
+@pytest.mark.parametrize("ld", [2050, 2049])
+def test_contract_gather_pitched_bit_exact(pnb, oracle, ld):
+    # 16-byte gathers (even pitch) and 8-byte gathers (odd pitch) of a padded 3x3 convolution
+    rng = np.random.default_rng(ld)
+    L, C, H = 2049, 2, 6
+    n_in = C * H * H
+    X = rng.integers(0, 1 << 63, (n_in, ld), dtype=np.uint64) * np.uint64(2)
+    W = rng.integers(-128, 128, (3, C * 9), dtype=np.int64)
+    idx = np.full((H * H, C * 9), -1, dtype=np.int32)
+    for oy in range(H):
+        for ox in range(H):
+            for c in range(C):
+                for ky in range(3):
+                    for kx in range(3):
+                        iy, ix = oy + ky - 1, ox + kx - 1
+                        if 0 <= iy < H and 0 <= ix < H:
+                            idx[oy * H + ox, c * 9 + ky * 3 + kx] = c * H * H + iy * H + ix
+    got = pnb.lwe_contract_gather_ld(torch.tensor(W.astype(np.int8), device="cuda"), None, 0,
+                                     torch.tensor(X.view(np.int64), device="cuda"),
+                                     torch.tensor(idx, device="cuda"), L)
+    got = got.cpu().numpy().view(np.uint64)[:, :, :L]
+    Xz = np.concatenate([X[:, :L], np.zeros((1, L), np.uint64)])
+    gathered = Xz[np.where(idx < 0, n_in, idx)]          # [G][K][L]
+    want = oracle.contract(W, None, 0, np.ascontiguousarray(gathered))
+    assert np.array_equal(got, want)
+    assert pnb.device_status(0) == 0
