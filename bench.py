@@ -59,9 +59,9 @@ WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussi
 # three times over the launch's seven block waves plus the small ciphertexts; 58.3 MB written).
 BR_TRAFFIC_PER_LAUNCH = 191380000 + 58270000
 # DRAM bytes (read + write) of one contract_tc_kernel launch of the contraction leg at 256
-# samples: the 32-sample ncu capture (411.4 MB read + 53.7 MB written, every input ciphertext
+# samples: the 32-sample ncu capture (411.8 MB read + 53.5 MB written, every input ciphertext
 # read once and every output written once) scaled by the 8x sample count.
-CONTRACT_TRAFFIC = 8 * (411416320 + 53726976)
+CONTRACT_TRAFFIC = 8 * (411782400 + 53461248)
 
 
 def load_package():
@@ -236,7 +236,8 @@ def contraction_leg(args, pnb, local, dev, flush):
                          (B * K * L * 8 / 1e9)},
         "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak["value"], "unit": "GB/s",
                      "frac": gbs / peak["value"], "peak_source": peak["source"],
-                     "kernel": "contract_tc_kernel", "algorithmic_bytes": algo_bytes,
+                     "kernel": "contract_tc_kernel<2> (TMA operand tiles)",
+                     "algorithmic_bytes": algo_bytes,
                      "traffic": CONTRACT_TRAFFIC},
     }
 
@@ -736,7 +737,7 @@ def run_gpu(args):
                 "frac": achieved / peak,
                 "peak_source": "FP64 FMA probe measured in this run (no FP64 entry in "
                                "MEASURED_PEAKS.json)",
-                "kernel": "blind_rotate_kernel<4>",
+                "kernel": "blind_rotate_tm_kernel<4>",
                 "traffic": BR_TRAFFIC_PER_LAUNCH}
 
     contraction = None if args.contract_batch <= 0 else contraction_leg(args, pnb, local, dev,
