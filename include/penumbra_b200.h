@@ -62,6 +62,15 @@ const char* pnb_last_error(void);
  * Replaces: keys::DEFAULT_PARAMS (runtime/src/keys.rs:29). */
 int pnb_params_default(pnb_params* out);
 
+/* Fill `out` with the library's 6-bit set at N = 8192: n=1024, k=1, N=8192, PBS 2^23 x 1 (2^15 x 2
+ * for low-noise bootstraps), KS 2^4 x 5, 3 message + 3 carry bits, small-key noise 2^-25, GLWE
+ * noise 2^-62 (fractions of the torus).  The reference names a 6-bit N=8192 set only in its
+ * benchmark configuration; these values are this library's choice (keyswitch + modulus-switch
+ * noise about 2^52.8 and single-level bootstrap noise about 2^50.5 against a 2^57 message scale).
+ * No reference counterpart (the reference's only set is keys::DEFAULT_PARAMS,
+ * runtime/src/keys.rs:29). */
+int pnb_params_n8192(pnb_params* out);
+
 /* Generate secret keys, the bootstrapping key (then its Fourier form) and the keyswitching key
  * on `device` from `seed`; blocks until the keys are resident.
  * Replaces: keys::keygen -> tfhe gen_keys_radix (runtime/src/keys.rs:47-56). */

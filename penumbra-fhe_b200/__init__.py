@@ -16,7 +16,7 @@ import os
 import torch
 
 __all__ = [
-    "Params", "default_params", "KeySet", "keygen", "lib", "LibraryError",
+    "Params", "default_params", "params_n8192", "KeySet", "keygen", "lib", "LibraryError",
     "encrypt", "phase", "decrypt_vec", "test_vector", "keyswitch", "keyswitch_workspace_bytes",
     "pbs_batch", "blind_rotate",
     "pbs_workspace_bytes", "lwe_contract", "lwe_contract_gather", "fft_negacyclic_mul", "measure_fp64_peak",
@@ -60,6 +60,7 @@ _SIGS = {
     "pnb_version": (C.c_int, []),
     "pnb_last_error": (C.c_char_p, []),
     "pnb_params_default": (C.c_int, [C.POINTER(Params)]),
+    "pnb_params_n8192": (C.c_int, [C.POINTER(Params)]),
     "pnb_keygen": (C.c_int, [C.c_int, C.POINTER(Params), C.c_uint64, C.POINTER(C.c_void_p)]),
     "pnb_keys_free": (C.c_int, [C.c_void_p]),
     "pnb_keys_import": (C.c_int, [C.c_int, C.POINTER(Params), C.c_void_p, C.c_void_p,
@@ -188,6 +189,13 @@ def _ptr(t: torch.Tensor | None) -> C.c_void_p:
 def default_params() -> Params:
     p = Params()
     _check("pnb_params_default", lib().pnb_params_default(C.byref(p)))
+    return p
+
+
+def params_n8192() -> Params:
+    """The library's 6-bit set at N = 8192 (``pnb_params_n8192``)."""
+    p = Params()
+    _check("pnb_params_n8192", lib().pnb_params_n8192(C.byref(p)))
     return p
 
 

@@ -127,6 +127,23 @@ int pnb_params_default(pnb_params* out) {
   return PNB_OK;
 }
 
+int pnb_params_n8192(pnb_params* out) {
+  if (!out) { set_error("out is NULL"); return PNB_ERR_INVALID; }
+  memset(out, 0, sizeof(*out));
+  out->n = 1024;
+  out->k = 1;
+  out->N = 8192;
+  out->pbs_base_log = 23;
+  out->pbs_level = 1;
+  out->ks_base_log = 4;
+  out->ks_level = 5;
+  out->msg_bits = 3;
+  out->carry_bits = 3;
+  out->lwe_std = 2.9802322387695312e-08;  // 2^-25
+  out->glwe_std = 2.168404344971009e-19;  // 2^-62
+  return PNB_OK;
+}
+
 int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** out) {
   if (!out) { set_error("out is NULL"); return PNB_ERR_INVALID; }
   *out = nullptr;
@@ -150,6 +167,8 @@ int pnb_keygen(int device, const pnb_params* params, uint64_t seed, pnb_keys** o
   rc = keygen_device(K, st);
   if (rc == PNB_OK && p.N == 2048) {
     rc = bsk_to_fourier(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), st);
+  } else if (rc == PNB_OK && p.N == 8192) {
+    rc = bsk_to_fourier_8k(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), st);
   }
   if (rc == PNB_OK) {
     e = cudaStreamSynchronize(st);
@@ -175,8 +194,8 @@ int pnb_keys_import(int device, const pnb_params* params, const uint64_t* lwe_sk
   }
   int rc = validate_params(params);
   if (rc) return rc;
-  if (params->N != 2048) {
-    set_error("pnb_keys_import: the Fourier conversion is compiled for N = 2048 (got %d)",
+  if (params->N != 2048 && params->N != 8192) {
+    set_error("pnb_keys_import: the Fourier conversion is compiled for N = 2048 and 8192 (got %d)",
               params->N);
     return PNB_ERR_UNSUPPORTED;
   }
@@ -208,7 +227,9 @@ int pnb_keys_import(int device, const pnb_params* params, const uint64_t* lwe_sk
                           8 * (size_t)(p.n + 1), rows, cudaMemcpyHostToDevice)) != cudaSuccess)
       rc = cuda_status(e, "pnb_keys_import(keyswitching key)");
   }
-  if (rc == PNB_OK) rc = bsk_to_fourier(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), 0);
+  if (rc == PNB_OK)
+    rc = p.N == 8192 ? bsk_to_fourier_8k(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), 0)
+                     : bsk_to_fourier(K->bsk, K->fbsk, (int)(K->bsk_words / p.N), 0);
   if (rc == PNB_OK && (e = cudaStreamSynchronize(0)) != cudaSuccess)
     rc = cuda_status(e, "pnb_keys_import synchronize");
   if (rc) {

@@ -112,6 +112,7 @@ __global__ void sk_ones_kernel(const uint64_t* glwe_sk, int k, int N, int* ones,
 
 // body += sum_c A_c * S_c (negacyclic, S binary), then the gadget term on row (comp, lev).
 // One block per GGSW row; the secret key enters as the list of its set positions.
+template <int PER>
 __global__ void __launch_bounds__(256) bsk_body_kernel(uint64_t* bsk, const int* ones_g,
                                                        const int* cnt_g,
                                                        const uint64_t* lwe_sk, int rows, int k,
@@ -123,8 +124,7 @@ __global__ void __launch_bounds__(256) bsk_body_kernel(uint64_t* bsk, const int*
   const int i = (int)(g / rows), r = (int)(g % rows);
   uint64_t* row = bsk + g * (size_t)(k + 1) * N;
   uint64_t* body = row + (size_t)k * N;
-  constexpr int PER = 16;  // outputs per thread (N <= 4096 with 256 threads)
-  uint64_t acc[PER];
+  uint64_t acc[PER];  // outputs per thread: N <= 256 PER
   const int per = (N + blockDim.x - 1) / blockDim.x;
 #pragma unroll
   for (int q = 0; q < PER; ++q) acc[q] = 0;
@@ -221,8 +221,8 @@ int keygen_device(pnb_keys* K, cudaStream_t st) {
   const pnb_params& p = K->p;
   const int big = p.k * p.N, rows = (p.k + 1) * p.pbs_level;
   const int nmax = big > p.n ? big : p.n;
-  if (p.N > 4096) {
-    set_error("keygen: the bootstrapping-key body kernel covers N <= 4096 (got %d)", p.N);
+  if (p.N > 8192) {
+    set_error("keygen: the bootstrapping-key body kernel covers N <= 8192 (got %d)", p.N);
     return PNB_ERR_UNSUPPORTED;
   }
   secret_keys_kernel<<<(nmax + 255) / 256, 256, 0, st>>>(K->lwe_sk, p.n, K->glwe_sk, big,
@@ -237,11 +237,19 @@ int keygen_device(pnb_keys* K, cudaStream_t st) {
   sk_ones_kernel<<<p.k, 32, 0, st>>>(K->glwe_sk, p.k, p.N, ones, ones + (size_t)p.k * p.N);
   PNB_CHECK_LAUNCH("sk_ones_kernel");
   const int smem = p.N * (int)sizeof(uint64_t) + p.N * (int)sizeof(int);
-  PNB_CUDA(cudaFuncSetAttribute(bsk_body_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                smem));
-  bsk_body_kernel<<<p.n * rows, 256, smem, st>>>(K->bsk, ones, ones + (size_t)p.k * p.N,
-                                                 K->lwe_sk, rows, p.k, p.N, p.pbs_level,
-                                                 p.pbs_base_log);
+  if (p.N <= 4096) {
+    PNB_CUDA(cudaFuncSetAttribute(bsk_body_kernel<16>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    bsk_body_kernel<16><<<p.n * rows, 256, smem, st>>>(K->bsk, ones, ones + (size_t)p.k * p.N,
+                                                       K->lwe_sk, rows, p.k, p.N, p.pbs_level,
+                                                       p.pbs_base_log);
+  } else {
+    PNB_CUDA(cudaFuncSetAttribute(bsk_body_kernel<32>,
+                                  cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    bsk_body_kernel<32><<<p.n * rows, 256, smem, st>>>(K->bsk, ones, ones + (size_t)p.k * p.N,
+                                                       K->lwe_sk, rows, p.k, p.N, p.pbs_level,
+                                                       p.pbs_base_log);
+  }
   PNB_CHECK_LAUNCH("bsk_body_kernel");
   PNB_CUDA(cudaFreeAsync(ones, st));
   ksk_kernel<<<big * p.ks_level, 128, 0, st>>>(K->ksk, K->glwe_sk, K->lwe_sk, p.n, K->ksk_row,

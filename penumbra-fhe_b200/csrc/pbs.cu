@@ -986,6 +986,7 @@ static int launch_ml_any(const pnb_keys* K, TvSel tv, const uint64_t* small, uin
 }
 
 static bool br_supported(const pnb_params& p) {
+  if (p.N == 8192) return br8k_supported(p);
   if (p.k != 1 || p.N != FFT_N || p.n > BR_MAXN || p.n <= 0) return false;
   if (p.pbs_level == 1) return p.pbs_base_log >= 2 && p.pbs_base_log <= 30;
   // multi-level: digits below 2^22 in magnitude keep the f64 product's error small, and the
@@ -1007,10 +1008,13 @@ int blind_rotate_sel(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_i
     set_error("blind rotation: test-vector period must be positive");
     return PNB_ERR_INVALID;
   }
+  if (K->p.N == 8192)
+    return blind_rotate_8k(K, tvs, tv_idx, period, tv_idx ? first % period : 0, small, out,
+                           out_ld == 0 ? K->p.N + 1 : out_ld, count, st);
   const TvSel tv{tvs, tv_idx, period, tv_idx ? first % period : 0};
   if (!br_supported(K->p)) {
-    set_error("blind rotation: compiled kernels cover k=1, N=2048, pbs_level 1..6 and (2^5, 9), "
-              "n<=%d (got "
+    set_error("blind rotation: compiled kernels cover k=1 with N=2048 (pbs_level 1..6 and "
+              "(2^5, 9), n<=%d) or N=8192 ((2^23, 1), (2^15, 2), (2^11, 4)) (got "
               "k=%d N=%d level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
               K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
@@ -1066,8 +1070,8 @@ size_t pbs_workspace_bytes(const pnb_keys* K, int count) {
 int pbs_batch(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
               int count, void* ws, size_t ws_bytes, cudaStream_t st) {
   if (!br_supported(K->p)) {
-    set_error("pbs: compiled kernels cover k=1, N=2048, pbs_level 1..6 and (2^5, 9), n<=%d (got "
-              "k=%d N=%d "
+    set_error("pbs: compiled kernels cover k=1 with N=2048 (pbs_level 1..6 and (2^5, 9), "
+              "n<=%d) or N=8192 ((2^23, 1), (2^15, 2), (2^11, 4)) (got k=%d N=%d "
               "level=%d base_log=%d n=%d)", BR_MAXN, K->p.k, K->p.N, K->p.pbs_level,
               K->p.pbs_base_log, K->p.n);
     return PNB_ERR_UNSUPPORTED;
@@ -1169,8 +1173,9 @@ __global__ void __launch_bounds__(32) fft_mul_kernel(const int64_t* __restrict__
 
 int fft_negacyclic_mul(int N, const int64_t* a, const uint64_t* b, uint64_t* out, int count,
                        cudaStream_t st) {
+  if (N == 8192) return fft_negacyclic_mul_8k(a, b, out, count, st);
   if (N != FFT_N) {
-    set_error("fft_negacyclic_mul: compiled for N = %d, got %d", FFT_N, N);
+    set_error("fft_negacyclic_mul: compiled for N = %d and 8192, got %d", FFT_N, N);
     return PNB_ERR_UNSUPPORTED;
   }
   if (count <= 0) return PNB_OK;

@@ -85,6 +85,33 @@ std::vector<KeyLevel> default_levels(int n, int N, int k, double glwe_std) {
   const bool is_default = (n == 834 && N == 2048 && k == 1 &&
                            std::fabs(glwe_std - 2.845267479601915e-15) < 1e-20);
   std::vector<KeyLevel> out;
+  if (N == 8192) {
+    // the gadgets compiled for N = 8192; noise: key noise through the digits, gadget rounding
+    // and the f64 product's error (relative 2^-51.1 of the product's spread, as measured at
+    // N = 2048), the last two amplified by the secret key (1 + kN/2 terms)
+    struct R8 {
+      int b, l;
+      double cost;
+    };
+    static const R8 r8[] = {{23, 1, 1.0}, {15, 2, 1.5}, {11, 4, 2.5}};
+    const double s = glwe_std * std::ldexp(1.0, 64);
+    for (const R8& r : r8) {
+      const double B = std::ldexp(1.0, r.b);
+      const double ed2 = B * B / 12.0;
+      const double v1 = (double)n * (k + 1) * r.l * N * ed2 * s * s;
+      const double eps = std::ldexp(1.0, 64 - r.b * r.l);
+      const double v2 = (n / 2.0) * (1 + k * N / 2.0) * eps * eps / 12.0;
+      const double sprod2 = std::exp2(-2 * 51.1) * N * ed2 * std::ldexp(1.0, 126) / 3.0;
+      const double v3 = (double)n * (1 + k * N / 2.0) * (k + 1) * r.l * sprod2;
+      KeyLevel L;
+      L.base_log = r.b;
+      L.level = r.l;
+      L.cost = r.cost;
+      L.log2_sigma = 0.5 * std::log2(v1 + v2 + v3);
+      out.push_back(L);
+    }
+    return out;
+  }
   for (const Row& r : rows) {
     KeyLevel L;
     L.base_log = r.b;

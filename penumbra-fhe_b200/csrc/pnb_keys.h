@@ -24,6 +24,15 @@ struct pnb_keys {
 namespace pnb {
 int keygen_device(pnb_keys* K, cudaStream_t st);
 int bsk_to_fourier(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaStream_t st);
+// N = 8192 (pbs8k.cu): Fourier conversion into the 4096-point transform's spectral order, and the
+// blind rotation + sample extraction of the 6-bit set.
+int bsk_to_fourier_8k(const uint64_t* bsk_dev, double2* fbsk_dev, int polys, cudaStream_t st);
+bool br8k_supported(const pnb_params& p);
+int fft_negacyclic_mul_8k(const int64_t* a, const uint64_t* b, uint64_t* out, int count,
+                          cudaStream_t st);
+int blind_rotate_8k(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_idx, int period,
+                    int first, const uint64_t* small, uint64_t* out, int out_ld, int count,
+                    cudaStream_t st);
 // Row pitches in words (`*_ld`, 0 = contiguous rows of the natural length) let the graph
 // evaluator keep its ciphertext rows 16-byte aligned.
 int keyswitch_launch(const pnb_keys* K, const uint64_t* in, uint64_t* out, int count,

@@ -97,6 +97,7 @@ def test_contract_gather_matches_im2col(pnb, oracle):
     (200, 130, 5, 2049, 2052),   # two M tiles, a wider pitch
     (33, 65, 2, 301, 302),       # ragged tiles
     (16, 72, 3, 2049, 2049),     # odd pitch: 8-byte gathers
+    (128, 256, 2, 8193, 8194),   # N = 8192 ciphertexts at their even pitch
 ])
 def test_contract_pitched_bit_exact(pnb, oracle, M, K, B, L, ld):
     rng = np.random.default_rng(M * 7 + K + ld)
