@@ -19,7 +19,10 @@ Per-configuration legs, at the end of the same line (the driver keeps the line's
             (strong scaling);
   "cnn"  -- configuration 5: the small CNN (tests/golden/cfg5_cnn.json) on `--cnn-batch` (64)
             samples per GPU, so 8 GPUs evaluate the configuration's 512-sample batch;
-  "linear_requant" -- configuration 3's Linear 784->128 + ReLU-Requant (N=2048 set);
+  "n8192" -- configuration 3 on the 6-bit N=8192 set: PBS/s, the Linear 784->128 contraction
+            over 8193-word ciphertexts (15.3 GB at 256 samples) against the HBM roofline, and
+            the Linear + ReLU-Requant graph end to end, every sample decrypt-checked;
+  "linear_requant" -- the same Linear + Requant graph on the N=2048 set;
   "contraction"    -- the encrypted Linear 784->128 (int4 weights, 256 samples of 784
                       ciphertexts) on the tensor cores against the HBM roofline;
   "noise"          -- the single-level bootstrap's output noise over ~1e5 bootstraps beside its
@@ -240,6 +243,83 @@ def contraction_leg(args, pnb, local, dev, flush):
                      "algorithmic_bytes": algo_bytes,
                      "traffic": CONTRACT_TRAFFIC},
     }
+
+
+def n8192_leg(args, pnb, world, rank, local, dist, dev, flush):
+    """Configuration 3 on the 6-bit set at N = 8192 (pnb_params_n8192): the bootstrap's PBS/s
+    (keyswitch + blind rotation, 64-entry LUT, decryption-checked), the Linear 784 -> 128
+    contraction over 8193-word ciphertexts against the HBM roofline (the 15.3 GB workload at 256
+    samples), and the Linear + ReLU-Requant graph end to end on `--n8k-batch` samples per GPU."""
+    import numpy as np
+    import torch
+    p = pnb.params_n8192()
+    keys = pnb.keygen(p, seed=SEED, device=local)
+    rng = np.random.default_rng(SEED + 81)
+    B = args.n8k_pbs_batch
+    lut = rng.integers(0, 64, 64)
+    msgs = rng.integers(0, 64, B)
+    tv = pnb.test_vector(keys, lut)
+    ct = pnb.encrypt(keys, torch.tensor(msgs), seed=SEED + 82)
+    small = torch.empty((B, p.n + 1), dtype=torch.int64, device=dev)
+    ks_ws = torch.empty(pnb.keyswitch_workspace_bytes(keys, B), dtype=torch.uint8, device=dev)
+    o = torch.empty_like(ct)
+    stream = torch.cuda.current_stream(dev)
+    pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+    pnb.blind_rotate(keys, tv, small, out=o)
+    ok = bool(np.array_equal(pnb.decrypt_vec(keys, o).cpu().numpy(), lut[msgs]))
+    ms = []
+    for _ in range(3):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        pnb.keyswitch(keys, ct, out=small, workspace=ks_ws)
+        pnb.blind_rotate(keys, tv, small, out=o)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        ms.append(a.elapsed_time(b))
+    pbs = {"batch": B, "pbs_per_second": B / (sum(ms) / len(ms) * 1e-3), "decrypt_ok": ok,
+           "params": {"n": p.n, "N": p.N, "pbs": [p.pbs_base_log, p.pbs_level],
+                      "ks": [p.ks_base_log, p.ks_level], "msg_bits": p.msg_bits,
+                      "carry_bits": p.carry_bits}}
+    del ct, small, ks_ws, o
+    keys.free()
+    # the contraction at d = 8192
+    M, K, Bc, L, LD = 128, 784, args.n8k_contract_batch, 8193, 8194
+    Wt = torch.tensor(rng.integers(-8, 8, (M, K)).astype(np.int8), device=dev)
+    bias = torch.tensor(rng.integers(-100, 100, M), device=dev)
+    X = torch.randint(-(1 << 62), 1 << 62, (Bc, K, LD), dtype=torch.int64, device=dev)
+    Y = torch.empty((Bc, M, LD), dtype=torch.int64, device=dev)
+    pnb.lwe_contract_ld(Wt, bias, 1 << 40, X, L, out=Y)
+    cms = []
+    for _ in range(5):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        pnb.lwe_contract_ld(Wt, bias, 1 << 40, X, L, out=Y)
+        b.record(stream)
+        torch.cuda.synchronize(dev)
+        cms.append(a.elapsed_time(b))
+    del X, Y
+    avg = sum(cms) / len(cms)
+    algo = Bc * K * L * 8 + Bc * M * L * 8 + M * K + M * 8
+    peak = _measured_hbm()
+    gbs = algo / (avg * 1e-3) / 1e9
+    contraction = {"workload": f"Linear {K}->{M}, int4 weights, {Bc} samples of {K} "
+                               f"ciphertexts of {L} words at a {LD}-word pitch",
+                   "ms": avg, "ms_median": statistics.median(cms), "algorithmic_bytes": algo,
+                   "roofline": {"bound": "hbm", "achieved": gbs, "peak": peak["value"],
+                                "unit": "GB/s", "frac": gbs / peak["value"],
+                                "peak_source": peak["source"],
+                                "floor_ms": algo / (peak["value"] * 1e9) * 1e3}}
+    graph = None
+    if args.n8k_batch > 0:
+        graph = graph_leg(args, pnb, world, rank, local, dist, dev, linear_requant_graph(),
+                          args.n8k_batch * world, SEED + 400,
+                          "Linear 784->128 (int4 weights U[-8,7]) + ReLU-Requant to 2 bits, "
+                          "6-bit inputs, 6-bit N=8192 parameter set",
+                          "encrypted_linear_requant_n8192_samples_per_second", "weak",
+                          params=p)
+    return {"pbs": pbs, "contraction": contraction, "linear_requant": graph}
 
 
 def _measured_hbm():
@@ -478,7 +558,7 @@ def program_cpu_baseline(plan, graph, per_level: int = 32):
 
 
 def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, seed, workload,
-              metric, scaling, cpu_baseline=None):
+              metric, scaling, cpu_baseline=None, params=None):
     """Encrypted inference of `graph` over `global_batch` samples sharded over the ranks
     (contiguous shards, `pnb.shard`): each rank encrypts and evaluates its shard on its own GPU
     (identical key replicas from one seed), one NCCL all-gather reassembles the output
@@ -490,7 +570,7 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, see
     import torch
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import ir_eval
-    plan = pnb.Plan(pnb.Graph(graph))
+    plan = pnb.Plan(pnb.Graph(graph), params=params)
     ev = pnb.Evaluator(plan, device=local, seed=SEED)  # identical keys on every rank
     hi = (1 << graph["input_bits"]) - 1
     x_all = np.random.default_rng(seed).integers(0, hi + 1, (global_batch, plan.input_elems))
@@ -747,6 +827,8 @@ def run_gpu(args):
              if (rank == 0 and args.noise) else None)
     sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
     key_sets = key_set_leg(pnb, dev, flush) if (rank == 0 and args.key_sets) else None
+    n8k = (n8192_leg(args, pnb, world, rank, local, dist, dev, flush)
+           if args.n8k else None)
     lin_rq = (None if args.lr_batch <= 0
               else linear_requant_leg(args, pnb, world, rank, local, dist, dev))
     cnn = None if args.cnn_batch <= 0 else cnn_leg(args, pnb, world, rank, local, dist, dev)
@@ -785,6 +867,7 @@ def run_gpu(args):
             "pbs_by_key_set": key_sets,
             "noise": noise,
             "contraction": contraction,
+            "n8192": n8k,
             "linear_requant": lin_rq,
             "cnn": cnn,
             "mlp": mlp,
@@ -849,6 +932,14 @@ def main():
     ap.add_argument("--mlp-batch", type=int, default=1024,
                     help="global batch of the encrypted MLP leg, sharded over the GPUs "
                          "(strong scaling; 0 skips it)")
+    ap.add_argument("--n8k", type=int, default=1,
+                    help="configuration 3 on the 6-bit N=8192 set (PBS/s, contraction, graph)")
+    ap.add_argument("--n8k-batch", type=int, default=8,
+                    help="samples per GPU of the N=8192 Linear 784->128 + Requant graph")
+    ap.add_argument("--n8k-pbs-batch", type=int, default=2048,
+                    help="bootstraps per launch of the N=8192 PBS measurement")
+    ap.add_argument("--n8k-contract-batch", type=int, default=256,
+                    help="samples of the N=8192 contraction (256: 15.3 GB of traffic)")
     ap.add_argument("--cnn-batch", type=int, default=64,
                     help="encrypted CNN samples per GPU (weak scaling; 0 skips the CNN leg)")
     ap.add_argument("--noise-cpu", type=int, default=8192,
