@@ -417,17 +417,6 @@ struct Builder {
                   }
                 R[(c * oh + oy) * ow + ox] = {to_i64(lo, where), to_i64(hi, where)};
               }
-          if (!op.pool_avg) {
-            int64_t lo = INT64_MAX, hi = INT64_MIN;
-            for (const auto& r : X) {
-              lo = std::min(lo, r.lo);
-              hi = std::max(hi, r.hi);
-            }
-            if (hi - lo > 3)
-              fail("node '" + nd.name + "': max pooling is implemented for inputs that take at "
-                   "most four values (a 2-bit activation); this input spans [" +
-                   std::to_string(lo) + ", " + std::to_string(hi) + "]");
-          }
           break;
         }
         case OpType::Requant: {
@@ -464,7 +453,7 @@ struct Builder {
         }
       }
       if (op.type == OpType::Linear || op.type == OpType::Conv2d ||
-          (op.type == OpType::Pool && op.pool_avg) || op.type == OpType::Add)
+          (op.type == OpType::Pool && (op.pool_avg || wide_max(X))) || op.type == OpType::Add)
         unite(t, tensor(nd.inputs[0]));
       range[t] = std::move(R);
       if (op.type == OpType::Linear || op.type == OpType::Conv2d) {
@@ -474,6 +463,25 @@ struct Builder {
               fail("node '" + nd.name + "': weight " + std::to_string(w) +
                    " does not fit the int8 tensor-core contraction");
       }
+    }
+  }
+
+  // Max pooling reads a tensor spanning at most four values with one pairwise lookup; wider
+  // tensors go through the digits of each pairwise difference (emit_maxpool_wide).
+  static bool wide_max(const std::vector<Range>& x) {
+    int64_t lo = INT64_MAX, hi = INT64_MIN;
+    for (const auto& r : x) {
+      lo = std::min(lo, r.lo);
+      hi = std::max(hi, r.hi);
+    }
+    return hi - lo > 3;
+  }
+  static void span_of(const std::vector<Range>& x, int64_t* lo, int64_t* hi) {
+    *lo = INT64_MAX;
+    *hi = INT64_MIN;
+    for (const auto& r : x) {
+      *lo = std::min(*lo, r.lo);
+      *hi = std::max(*hi, r.hi);
     }
   }
 
@@ -613,8 +621,15 @@ struct Builder {
       const int yt = tensor(nd.inputs[0]);
       for (const Pair& p : pairs[ni])
         tighten(yt, range[yt][p.e].lo - p.T, range[yt][p.e].hi - p.T);
-      if (nd.op.type == OpType::Activation || (nd.op.type == OpType::Pool && !nd.op.pool_avg))
+      if (nd.op.type == OpType::Pool && !nd.op.pool_avg && wide_max(range[yt])) {
+        // the pairwise differences a - b are split into digits at the input's scale
+        int64_t lo, hi;
+        span_of(range[yt], &lo, &hi);
+        tighten(yt, lo - hi, hi - lo);
+      } else if (nd.op.type == OpType::Activation ||
+                 (nd.op.type == OpType::Pool && !nd.op.pool_avg)) {
         cap[find(yt)] = std::min(cap[find(yt)], 59);
+      }
     }
     // A Requant reading a class rooted at a graph input sees fresh (tiny) noise, so the single
     // z = mult*y + rb chain is affordable there: leave room for z's wider range.
@@ -697,6 +712,8 @@ struct Builder {
         case OpType::Pool:
           if (op.pool_avg)
             vmax[in] = std::min(vmax[in], vmax[out] / (op.pool_h * op.pool_w));
+          else if (wide_max(range[in]))  // a - b read in 2-bit windows (emit_maxpool_wide)
+            vmax[in] = std::min(vmax[in], 0.25 * allowed(62, scale[in]));
           else  // read as 4a + b at cells of 2^59 (see emit_maxpool)
             vmax[in] = std::min(vmax[in], 0.9 * allowed(59, scale[in]) / 17.0);
           break;
@@ -822,7 +839,8 @@ struct Builder {
       case OpType::Conv2d:
       case OpType::Pool: {
         if (op.type == OpType::Pool && !op.pool_avg) {
-          emit_maxpool(ni, rep);
+          if (wide_max(range[in])) emit_maxpool_wide(ni, rep);
+          else emit_maxpool(ni, rep);
           return;
         }
         Instr I;
@@ -1026,6 +1044,164 @@ struct Builder {
     snprintf(line, sizeof line, "%-20s Pool(max)  %lld bootstraps/elem over %d tree levels, key %s\n",
              nd.name.c_str(), (long long)(pbs_count / std::max<int64_t>(E, 1)), level_no,
              key_name(fl).c_str());
+    rep << line;
+  }
+
+  // Max pooling of wide values: a pairwise tree, max(a, b) = b + relu(a - b).  The difference d
+  // is split LSB first into nd two's-complement digits of 2 bits (the radix split's peeling:
+  // each window read through the negacyclic sign and a two-box lookup, once at the running
+  // scale to clear the digit and once at 2^59 to form the digit g_i * 2^59); the top window's
+  // sign read also emits s * 2^61, s = [d >= 0].  One lookup per digit on g_i 2^59 + s 2^61
+  // (eight cells of 2^59) emits s g_i 4^i at the input's scale, and relu(d) is their sum (for
+  // d >= 0 the top digit is 0 or 1; for d < 0 every term is 0).  Inner maxima stay at the
+  // input's scale.
+  void emit_maxpool_wide(int ni, std::ostringstream& rep) {
+    const auto& nd = g.nodes[ni];
+    const auto& op = nd.op;
+    const int out = tensor(nd.outputs[0]);
+    const int in = tensor(nd.inputs[0]);
+    const int64_t E = (int64_t)range[out].size();
+    const int ex = scale[in];
+    if (scale[out] != ex) fail("internal: wide max pooling keeps the input's scale");
+    int64_t lo, hi;
+    span_of(range[in], &lo, &hi);
+    const int ndg = (bits_signed(lo - hi, hi - lo) + 1) / 2;  // 2-bit digits of a - b
+    if (ex + 2 * ndg > 64) fail("node '" + nd.name + "': no room for the differences' digits");
+    const int oh = (op.in_h - op.pool_h) / op.stride + 1;
+    const int ow = (op.in_w - op.pool_w) / op.stride + 1;
+    struct Opd {
+      int buf;
+      std::vector<int32_t> map;  // per output element (empty: identity)
+      double V;
+    };
+    std::vector<Opd> ops;
+    for (int ky = 0; ky < op.pool_h; ++ky)
+      for (int kx = 0; kx < op.pool_w; ++kx) {
+        Opd d{buf[in], std::vector<int32_t>(E), var[in]};
+        for (int c = 0; c < op.channels; ++c)
+          for (int oy = 0; oy < oh; ++oy)
+            for (int ox = 0; ox < ow; ++ox)
+              d.map[(c * oh + oy) * ow + ox] = c * op.in_h * op.in_w +
+                                               (oy * op.stride + ky) * op.in_w + ox * op.stride +
+                                               kx;
+        ops.push_back(std::move(d));
+      }
+    const int l0 = lvl_order[0];
+    const double v_inner = 0.25 * allowed(62, ex);  // what an inner maximum may carry
+    const int64_t pbs_before = P.pbs_per_sample;
+    if (ops.size() == 1) {
+      lin(buf[out], {Term{ops[0].buf, {1}, ops[0].map}}, {0}, nd.name + ": 1x1 window");
+      var[out] = ops[0].V;
+      return;
+    }
+    // scratch, shared by every pair
+    const int R = new_buf(E, nd.name + ".d");
+    const int Xc = new_buf(E, nd.name + ".clear");
+    const int Xb = new_buf(E, nd.name + ".bit");
+    const int Yb = new_buf(E, nd.name + ".low");
+    const int S = new_buf(E, nd.name + ".sign");
+    const int G = new_buf(E * ndg, nd.name + ".digits");
+    const int W = new_buf(E * ndg, nd.name + ".terms");
+    std::string keys;
+    while (ops.size() > 1) {
+      const bool last = ops.size() == 2;
+      std::vector<Opd> next;
+      for (size_t j = 0; j + 1 < ops.size(); j += 2) {
+        const Opd& a = ops[j];
+        const Opd& b = ops[j + 1];
+        const double Vd = a.V + b.V;
+        lin(R, {Term{a.buf, {1}, a.map}, Term{b.buf, {-1}, b.map}}, {0}, nd.name + ": a - b");
+        Chain c{R, Xc, E, ex, Vd};
+        std::vector<int> ws(ndg, 2), lv;
+        double Vend = 0, cost = 0;
+        if (!eval_windows(c, ws, 64, &lv, &Vend, &cost))
+          fail("node '" + nd.name + "': max pooling input too noisy for exact differences");
+        for (int i = 0; i < ndg; ++i) {
+          const int Ei = ex + 2 * i;
+          const int shift = 62 - Ei;
+          const bool top = i == ndg - 1;
+          std::vector<int32_t> gm(E * ndg, -1);
+          for (int64_t e = 0; e < E; ++e) gm[e * ndg + i] = (int32_t)e;
+          std::vector<uint64_t> gc(E * ndg, 0);
+          for (int64_t e = 0; e < E; ++e) gc[e * ndg + i] = pow2(59);
+          pbs(Xb, R, shift, pow2(61), l0, {tv(const_tv(pow2(59)))}, E, nd.name + ": digit sign");
+          if (top)
+            pbs(S, R, shift, pow2(61), l0, {tv(const_tv(pow2(60)))}, E, nd.name + ": sign of d");
+          pbs(Xc, R, shift, pow2(61), lv[2 * i], {tv(const_tv(pow2(Ei)))}, E,
+              nd.name + ": clear digit sign");
+          lin(R, {Term{R, {1}, {}}, Term{Xc, {1}, {}}}, {(uint64_t)0 - pow2(Ei)},
+              nd.name + ": clear top bit");
+          TvSpec lb;
+          lb.lut_len = 2;
+          lb.val = {0, pow2(59)};
+          pbs(Yb, R, shift, 0, l0, {tv(lb)}, E, nd.name + ": digit low bit");
+          // G[e][i] = (2^59 - Xb) + Yb = g_i 2^59
+          if (i == 0) {  // the first digit also clears the other digits' slots
+            lin(G, {Term{Xb, {-1}, gm}, Term{Yb, {1}, gm}}, gc, nd.name + ": digit");
+          } else {
+            std::vector<int32_t> gid(E * ndg);
+            for (int64_t q = 0; q < E * ndg; ++q) gid[q] = (int32_t)q;
+            lin(G, {Term{G, {1}, gid}, Term{Xb, {-1}, gm}, Term{Yb, {1}, gm}}, gc,
+                nd.name + ": digit");
+          }
+          if (!top) {
+            TvSpec lc;
+            lc.lut_len = 2;
+            lc.val = {0, pow2(Ei)};
+            pbs(Xc, R, shift, 0, lv[2 * i + 1], {tv(lc)}, E, nd.name + ": clear low bit");
+            lin(R, {Term{R, {1}, {}}, Term{Xc, {-1}, {}}}, {0}, nd.name + ": clear low bit");
+          }
+        }
+        // the terms s g_i 4^i at the input's scale: one lookup per digit on g_i 2^59 + s 2^61;
+        // S = (sign read + 2^60) = s 2^61
+        std::vector<int32_t> rep_s(E * ndg);
+        for (int64_t q = 0; q < E * ndg; ++q) rep_s[q] = (int32_t)(q / ndg);
+        lin(G, {Term{G, {1}, {}}, Term{S, {1}, rep_s}}, {pow2(60)}, nd.name + ": digit + sign");
+        const double v_target = last ? vmax[out] : v_inner;
+        int lt = -1;
+        for (int l : lvl_order)
+          if (b.V + ndg * lvar(l) <= 0.9 * v_target) {
+            lt = l;
+            break;
+          }
+        if (lt < 0) fail("node '" + nd.name + "': no key set is precise enough for max pooling");
+        std::vector<int32_t> tvi(E * ndg);
+        std::vector<int> tv_of(ndg);
+        for (int i = 0; i < ndg; ++i) {
+          TvSpec sp;
+          sp.lut_len = 16;
+          for (int v = 0; v < 16; ++v) {
+            const int gdig = v & 3, sbit = (v >> 2) & 1;
+            sp.val.push_back(v < 8 && sbit ? ((uint64_t)gdig << (2 * i)) << ex : 0);
+          }
+          tv_of[i] = tv(sp);
+        }
+        for (int64_t q = 0; q < E * ndg; ++q) tvi[q] = tv_of[q % ndg];
+        pbs(W, G, 0, 0, lt, tvi, E * ndg, nd.name + ": s * digit");
+        // max = b + sum of terms, into a fresh buffer (or the output)
+        const int Y = last ? buf[out] : new_buf(E, nd.name + ".max");
+        for (int i0 = 0; i0 < ndg; i0 += 2) {
+          std::vector<Term> terms;
+          terms.push_back(i0 == 0 ? Term{b.buf, {1}, b.map} : Term{Y, {1}, {}});
+          for (int i = i0; i < std::min(ndg, i0 + 2); ++i) {
+            std::vector<int32_t> m(E);
+            for (int64_t e = 0; e < E; ++e) m[e] = (int32_t)(e * ndg + i);
+            terms.push_back(Term{W, {1}, m});
+          }
+          lin(Y, terms, {0}, nd.name + ": b + relu(a - b)");
+        }
+        keys = key_name(lt);
+        next.push_back(Opd{Y, {}, b.V + ndg * lvar(lt)});
+      }
+      if (ops.size() % 2) next.push_back(ops.back());
+      ops = std::move(next);
+    }
+    var[out] = ops[0].V;
+    char line[256];
+    snprintf(line, sizeof line,
+             "%-20s Pool(max)  %lld bootstraps/elem, differences in %d 2-bit digits, terms %s\n",
+             nd.name.c_str(), (long long)((P.pbs_per_sample - pbs_before) / std::max<int64_t>(E, 1)),
+             ndg, keys.c_str());
     rep << line;
   }
 

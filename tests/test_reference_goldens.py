@@ -53,6 +53,11 @@ def _cases():
         _g([{"name": "pool", "inputs": ["x"], "outputs": ["y"],
              "op": {"op_type": "Pool", "mode": "avg", "in_h": 4, "in_w": 4, "channels": 2,
                     "pool_h": 2, "pool_w": 2, "stride": 2}}], ["x"], ["y"], 6, 5), [x], None)
+    # golden_pool.rs (max): the same map and window, the window maximum of wide values
+    cases["pool_max"] = (
+        _g([{"name": "pool", "inputs": ["x"], "outputs": ["y"],
+             "op": {"op_type": "Pool", "mode": "max", "in_h": 4, "in_w": 4, "channels": 2,
+                    "pool_h": 2, "pool_w": 2, "stride": 2}}], ["x"], ["y"], 6, 5), [x], None)
     # runtime/tests/golden_add.rs: a = [3, -5], b = [4, 6]
     cases["add"] = (
         _g([{"name": "add", "inputs": ["a", "b"], "outputs": ["sum"],
@@ -126,13 +131,16 @@ def test_reference_golden_encrypted(pnb, name):
     assert pnb.device_status(0) == 0
 
 
-def test_max_pool_is_reported_unsupported(pnb):
-    # runtime/tests/golden_pool.rs also runs mode "max"; this path rejects it with a message
-    g = _g([{"name": "pool", "inputs": ["x"], "outputs": ["y"],
-             "op": {"op_type": "Pool", "mode": "max", "in_h": 4, "in_w": 4, "channels": 2,
-                    "pool_h": 2, "pool_w": 2, "stride": 2}}], ["x"], ["y"], 6, 5)
-    with pytest.raises(pnb.LibraryError, match="max"):
-        pnb.Plan(pnb.Graph(g), input_range=(-31, 31))
+def test_max_pool_of_wide_values_random_inputs(pnb):
+    # golden_pool.rs's max mode over inputs spanning 63 values: the digit-wise program equals
+    # the window maximum on random inputs too
+    g, _, lens = CASES["pool_max"]
+    plan = _plan(pnb, g, lens)
+    xs = np.random.default_rng(7).integers(-31, 32, (32, 32))
+    y, margin = plan.simulate(xs)
+    for x, got in zip(xs, y):
+        assert got.tolist() == _expect(g, x.tolist(), lens)
+    assert margin >= 63.5
 
 
 def _linear_requant_graph():
