@@ -1,8 +1,8 @@
 """Generate the committed golden fixtures from the reference's own Python code.
 
-Run in a checkout that has the reference at REF (default /root/reference):
+Run with the path of a reference checkout (Harikeshav-R/Penumbra-FHE) as the argument:
 
-    python tests/golden/make_golden.py [REF]
+    python tests/golden/make_golden.py REF
 
 For every benchmark configuration it builds the model with the reference quantizer
 (``python/penumbra/model.py`` ``Model.quantize``) on seeded synthetic data, quantizes seeded
@@ -33,7 +33,9 @@ import types
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-REF = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+if len(sys.argv) != 2:
+    sys.exit("usage: python tests/golden/make_golden.py <path of a reference checkout>")
+REF = sys.argv[1]
 
 
 def _import_reference():
