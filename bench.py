@@ -285,6 +285,8 @@ def n8192_leg(args, pnb, world, rank, local, dist, dev, flush):
     keys.free()
     # the contraction at d = 8192
     M, K, Bc, L, LD = 128, 784, args.n8k_contract_batch, 8193, 8194
+    if Bc <= 0:
+        return {"pbs": pbs, "contraction": None, "linear_requant": None}
     Wt = torch.tensor(rng.integers(-8, 8, (M, K)).astype(np.int8), device=dev)
     bias = torch.tensor(rng.integers(-100, 100, M), device=dev)
     X = torch.randint(-(1 << 62), 1 << 62, (Bc, K, LD), dtype=torch.int64, device=dev)
