@@ -92,6 +92,22 @@ int pnb_keys_info(const pnb_keys* keys, pnb_params* params_out, int* device_out,
 int pnb_keys_export(const pnb_keys* keys, uint64_t* lwe_sk_host, uint64_t* glwe_sk_host,
                     uint64_t* bsk_host, uint64_t* ksk_host);
 
+/* Byte containers (little-endian, versioned, self-describing) for shipping keys and ciphertexts
+ * between a client and a GPU server.  A key set serialises its parameters, its standard-domain
+ * bootstrapping key and keyswitching key (pnb_keys_export's layouts) and, with with_secrets,
+ * the secret keys; deserialising computes the Fourier key on `device` (without secrets: an
+ * evaluation-key set).  Ciphertext batches are [count][dim+1] u64 rows (mask, then body) in host
+ * memory; pnb_lwe_deserialize with ct_host = NULL returns count and dim only.  The reference
+ * serialises nothing (keys.rs:47-56 generates them in-process); tfhe-rs's own serialized format
+ * cannot be checked here (the crate is absent), so these containers are this library's own. */
+size_t pnb_keys_serialized_bytes(const pnb_keys* keys, int with_secrets);
+int pnb_keys_serialize(const pnb_keys* keys, int with_secrets, void* out_host, size_t cap);
+int pnb_keys_deserialize(int device, const void* in_host, size_t len, pnb_keys** out);
+size_t pnb_lwe_serialized_bytes(int count, int dim);
+int pnb_lwe_serialize(const uint64_t* ct_host, int count, int dim, void* out_host, size_t cap);
+int pnb_lwe_deserialize(const void* in_host, size_t len, uint64_t* ct_host, size_t cap_words,
+                        int* count, int* dim);
+
 /* Client side (test harness).  Encrypt messages[i]*delta under the big (k*N) key with GLWE
  * noise; ciphertext i uses keystream index first_index+i of `seed`.
  * Replaces: encrypt::encrypt -> RadixClientKey::encrypt_signed (runtime/src/encrypt.rs:20-22). */

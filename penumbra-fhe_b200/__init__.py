@@ -23,7 +23,8 @@ __all__ = [
     "device_status", "pbs_batch_noalloc", "Graph", "Plan", "Evaluator", "shard",
     "gather_shards", "evaluate_sharded", "op_bits", "wait_probe", "import_keys", "radix_merge",
     "TensorDesc", "KeyRing", "op_plan", "requant_batch", "argmax_batch", "add_batch",
-    "radix_plan", "lwe_contract_ld", "lwe_contract_gather_ld",
+    "radix_plan", "lwe_contract_ld", "lwe_contract_gather_ld", "deserialize_keys",
+    "serialize_lwe", "deserialize_lwe",
 ]
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
@@ -97,6 +98,13 @@ _SIGS = {
     "pnb_lwe_contract_gather_ld": (C.c_int, [C.c_void_p, C.c_void_p, C.c_uint64, C.c_int,
                                              C.c_int, C.c_void_p, C.c_int, C.c_void_p, C.c_int,
                                              C.c_void_p, C.c_int, C.c_int, C.c_void_p]),
+    "pnb_keys_serialized_bytes": (C.c_size_t, [C.c_void_p, C.c_int]),
+    "pnb_keys_serialize": (C.c_int, [C.c_void_p, C.c_int, C.c_void_p, C.c_size_t]),
+    "pnb_keys_deserialize": (C.c_int, [C.c_int, C.c_void_p, C.c_size_t, C.POINTER(C.c_void_p)]),
+    "pnb_lwe_serialized_bytes": (C.c_size_t, [C.c_int, C.c_int]),
+    "pnb_lwe_serialize": (C.c_int, [C.c_void_p, C.c_int, C.c_int, C.c_void_p, C.c_size_t]),
+    "pnb_lwe_deserialize": (C.c_int, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t,
+                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]),
     "pnb_fft_negacyclic_mul": (C.c_int, [C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p,
                                          C.c_int, C.c_void_p]),
     "pnb_measure_fp64_peak": (C.c_int, [C.c_int, C.POINTER(C.c_double)]),
@@ -241,6 +249,15 @@ class KeySet:
                                    C.byref(kb)))
         return {"device": dev.value, "fourier_bsk_bytes": fb.value, "ksk_bytes": kb.value}
 
+    def serialize(self, with_secrets: bool = False) -> bytes:
+        """The key set as a byte container (``pnb_keys_serialize``); without secrets it carries
+        the evaluation keys only."""
+        n = lib().pnb_keys_serialized_bytes(self.handle, int(with_secrets))
+        buf = C.create_string_buffer(n)
+        _check("pnb_keys_serialize", lib().pnb_keys_serialize(self.handle, int(with_secrets),
+                                                              buf, n))
+        return buf.raw
+
     def export(self, lwe_sk=True, glwe_sk=True, bsk=False, ksk=False) -> dict:
         """Copy key material to host numpy arrays (blocking)."""
         import numpy as np
@@ -287,6 +304,45 @@ def import_keys(params: Params, keys: dict, device: int = 0) -> KeySet:
     _check("pnb_keys_import",
            lib().pnb_keys_import(device, C.byref(params), *bufs, C.byref(h)))
     return KeySet(h, params, device, 0)
+
+
+def deserialize_keys(data: bytes, device: int = 0) -> KeySet:
+    """A key set from ``KeySet.serialize`` bytes (``pnb_keys_deserialize``)."""
+    h = C.c_void_p()
+    _check("pnb_keys_deserialize", lib().pnb_keys_deserialize(device, data, len(data),
+                                                              C.byref(h)))
+    p, dev = Params(), C.c_int()
+    fb, kb = C.c_size_t(), C.c_size_t()
+    _check("pnb_keys_info", lib().pnb_keys_info(h, C.byref(p), C.byref(dev), C.byref(fb),
+                                                C.byref(kb)))
+    return KeySet(h, p, device, 0)
+
+
+def serialize_lwe(ct) -> bytes:
+    """LWE ciphertexts [count, dim+1] (torch tensor or numpy array) as a byte container."""
+    import numpy as np
+    a = ct.cpu().numpy() if isinstance(ct, torch.Tensor) else np.asarray(ct)
+    a = np.ascontiguousarray(a.reshape(-1, a.shape[-1])).view(np.uint64)
+    count, dim = a.shape[0], a.shape[1] - 1
+    n = lib().pnb_lwe_serialized_bytes(count, dim)
+    buf = C.create_string_buffer(n)
+    _check("pnb_lwe_serialize", lib().pnb_lwe_serialize(C.c_void_p(a.ctypes.data), count, dim,
+                                                        buf, n))
+    return buf.raw
+
+
+def deserialize_lwe(data: bytes):
+    """Ciphertexts [count, dim+1] (numpy u64) from ``serialize_lwe`` bytes."""
+    import numpy as np
+    count, dim = C.c_int(), C.c_int()
+    _check("pnb_lwe_deserialize", lib().pnb_lwe_deserialize(data, len(data), None, 0,
+                                                            C.byref(count), C.byref(dim)))
+    out = np.zeros((count.value, dim.value + 1), dtype=np.uint64)
+    _check("pnb_lwe_deserialize", lib().pnb_lwe_deserialize(data, len(data),
+                                                            C.c_void_p(out.ctypes.data),
+                                                            out.size, C.byref(count),
+                                                            C.byref(dim)))
+    return out
 
 
 def _u64(t: torch.Tensor) -> torch.Tensor:

@@ -223,3 +223,24 @@ def test_imported_evaluation_keys_bootstrap_identically(pnb, gkeys):
     full = pnb.import_keys(gkeys.params, ex, device=0)
     assert torch.equal(pnb.encrypt(full, torch.tensor(msgs), seed=9), ct)
     assert pnb.device_status(0) == 0
+
+
+def test_serialized_keys_bootstrap_bit_identically(pnb, gkeys):
+    # evaluation keys shipped as bytes (no secrets) bootstrap exactly as the original set; the
+    # container with secrets restores a client set that encrypts identically
+    rng = np.random.default_rng(44)
+    msgs = rng.integers(0, 16, 64)
+    lut = rng.integers(0, 16, 16)
+    ct = pnb.encrypt(gkeys, torch.tensor(msgs), seed=45)
+    tv = pnb.test_vector(gkeys, lut)
+    want = pnb.pbs_batch(gkeys, tv, ct)
+    server = pnb.deserialize_keys(gkeys.serialize(with_secrets=False), device=0)
+    got = pnb.pbs_batch(server, pnb.test_vector(server, lut), ct)
+    assert torch.equal(got, want)
+    with pytest.raises(pnb.LibraryError):
+        pnb.encrypt(server, torch.tensor(msgs), seed=45)
+    client = pnb.deserialize_keys(gkeys.serialize(with_secrets=True), device=0)
+    assert torch.equal(pnb.encrypt(client, torch.tensor(msgs), seed=45), ct)
+    back = pnb.deserialize_lwe(pnb.serialize_lwe(ct))
+    assert np.array_equal(back, _u64(ct))
+    assert pnb.device_status(0) == 0
