@@ -423,6 +423,19 @@ __device__ __forceinline__ double2 words_to_d2(const uint32_t* t) {
                       __hiloint2double((int)t[3], (int)t[2]));
 }
 
+// round(w) mod 2^32 for w = v 2^-32 (|w| < 2^63): with PNB_BR_F2I one conversion to a 64-bit
+// integer (off the FP64 pipe), otherwise scaled_f64_to_top32's three FP64 operations.
+#ifndef PNB_BR_F2I
+#define PNB_BR_F2I 1
+#endif
+__device__ __forceinline__ uint32_t top32_round(double w) {
+#if PNB_BR_F2I
+  return (uint32_t)(unsigned long long)__double2ll_rn(w);
+#else
+  return scaled_f64_to_top32(w);
+#endif
+}
+
 // Complex values per tensor-memory round trip in the rotation (4: 16 columns, 8: 32 columns);
 // tcgen05.wait::ld waits for every load in flight, so a round trip is one load and one wait.
 #ifndef PNB_BR_TM_CHUNK
@@ -567,9 +580,10 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
         const int e = r * 32 + lane;
         const double2 fo = f_own[e], ft = f_oth[e];
         const double2 dt = words_to_d2(t + 4 * q);
-        const double2 p0 = cmul(x[r], fo);
-        x[r] = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
-                            p0.y + fma(dt.x, ft.y, dt.y * ft.x));
+        // x fo + dt ft as one chain of fused multiply-adds per component (8 FP64 operations)
+        const double2 xv = x[r];
+        x[r] = make_double2(fma(xv.x, fo.x, fma(-xv.y, fo.y, fma(dt.x, ft.x, -dt.y * ft.y))),
+                            fma(xv.x, fo.y, fma(xv.y, fo.x, fma(dt.x, ft.y, dt.y * ft.x))));
       }
     }
     // Every warp is done with GGSW i and with the other warp's spectrum: stage GGSW i+1 while
@@ -603,8 +617,8 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
       uint2 o = acc2[j];
-      o.x += scaled_f64_to_top32(x[m].x);
-      o.y += scaled_f64_to_top32(x[m].y);
+      o.x += top32_round(x[m].x);
+      o.y += top32_round(x[m].y);
       acc2[j] = o;
     }
     __syncwarp();
