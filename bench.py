@@ -32,9 +32,10 @@ Per-configuration legs, at the end of the same line (the driver keeps the line's
 Every graph leg decrypts every sample on rank 0 and compares it with the cleartext graph.
 
 N > 1 runs one process per GPU under torchrun; in the PBS leg each rank bootstraps its own 4096
-ciphertexts against its own key replica and one NCCL all-gather per step reassembles the
-layer's outputs on every rank (weak scaling), time = max over ranks.  The graph legs shard
-samples over ranks and reassemble the output ciphertexts with one NCCL all-gather.
+ciphertexts against its own key replica and one all-gather per step (the library's
+pnb_allgather over NCCL) reassembles the layer's outputs on every rank (weak scaling), time =
+max over ranks.  The graph legs shard samples over ranks and reassemble the output ciphertexts
+with one pnb_allgather.
 `--impl reference` times the CPU restatement of the same PBS (the oracle's unvectorised f64 FFT
 path, the algorithm tfhe-rs runs on the CPU) on all host cores; it needs no GPU.
 """
@@ -141,8 +142,8 @@ def dist_setup(args):
 def pbs_config(batch: int, world: int) -> dict:
     """The PBS microbenchmark's `config` (both arms print the same one)."""
     return {"workload": WORKLOAD, "batch_per_gpu": batch, "global_batch": batch * world,
-            "parallelism": (f"ciphertexts sharded over {world} GPUs, outputs all-gathered over "
-                            "NCCL every step" if world > 1 else "one GPU"),
+            "parallelism": (f"ciphertexts sharded over {world} GPUs, outputs all-gathered "
+                            "(pnb_allgather over NCCL) every step" if world > 1 else "one GPU"),
             "l2": "flushed (256 MB write) between timed steps"}
 
 
@@ -245,7 +246,7 @@ def contraction_leg(args, pnb, local, dev, flush):
     }
 
 
-def n8192_leg(args, pnb, world, rank, local, dist, dev, flush):
+def n8192_leg(args, pnb, world, rank, local, dist, dev, flush, comm=None):
     """Configuration 3 on the 6-bit set at N = 8192 (pnb_params_n8192): the bootstrap's PBS/s
     (keyswitch + blind rotation, 64-entry LUT, decryption-checked), the Linear 784 -> 128
     contraction over 8193-word ciphertexts against the HBM roofline (the 15.3 GB workload at 256
@@ -320,7 +321,7 @@ def n8192_leg(args, pnb, world, rank, local, dist, dev, flush):
                           "Linear 784->128 (int4 weights U[-8,7]) + ReLU-Requant to 2 bits, "
                           "6-bit inputs, 6-bit N=8192 parameter set",
                           "encrypted_linear_requant_n8192_samples_per_second", "weak",
-                          params=p)
+                          params=p, comm=comm)
     return {"pbs": pbs, "contraction": contraction, "linear_requant": graph}
 
 
@@ -560,10 +561,10 @@ def program_cpu_baseline(plan, graph, per_level: int = 32):
 
 
 def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, seed, workload,
-              metric, scaling, cpu_baseline=None, params=None):
+              metric, scaling, cpu_baseline=None, params=None, comm=None):
     """Encrypted inference of `graph` over `global_batch` samples sharded over the ranks
     (contiguous shards, `pnb.shard`): each rank encrypts and evaluates its shard on its own GPU
-    (identical key replicas from one seed), one NCCL all-gather reassembles the output
+    (identical key replicas from one seed), one pnb_allgather reassembles the output
     ciphertexts on every rank.  `value` = global_batch / (max over ranks of the device time of
     evaluation + all-gather); `e2e` adds this rank's host->device input copy and rank 0's
     device->host copy of the gathered outputs.  Rank 0 decrypts EVERY sample and compares it
@@ -597,7 +598,7 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, see
     evs[1].record(stream)
     out = ev.evaluate(d_in)
     evs[2].record(stream)
-    gathered = pnb.gather_shards(out, global_batch) if dist is not None else out
+    gathered = pnb.gather_shards(out, global_batch, comm=comm) if dist is not None else out
     evs[3].record(stream)
     if rank == 0:
         h_out.copy_(gathered, non_blocking=True)
@@ -623,7 +624,7 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, see
         "global_batch": global_batch, "samples_per_gpu": B, "scaling": scaling, "ms": t_dev,
         "config": {"workload": workload,
                    "parallelism": f"samples sharded over {world} GPU(s), outputs all-gathered "
-                                  "over NCCL"},
+                                  "(pnb_allgather over NCCL)"},
         "bootstraps_per_sample": plan.pbs_per_sample,
         "bootstraps_by_key_set": [[bl, lv, c] for bl, lv, c in plan.key_sets()],
         "cpu_baseline": (cpu_baseline(plan, graph) if cpu_baseline is not None and rank == 0
@@ -636,7 +637,7 @@ def graph_leg(args, pnb, world, rank, local, dist, dev, graph, global_batch, see
     }
 
 
-def mlp_leg(args, pnb, world, rank, local, dist, dev):
+def mlp_leg(args, pnb, world, rank, local, dist, dev, comm=None):
     """Encrypted MLP 784-128-128-10 (the reference quantizer's graph for that configuration) on
     a fixed global batch sharded over the ranks (strong scaling)."""
     with open(os.path.join(ROOT, "tests", "golden", "cfg4_mlp.json")) as f:
@@ -646,10 +647,10 @@ def mlp_leg(args, pnb, world, rank, local, dist, dev):
                      "MLP 784-128-128-10, ReLU fused in Requant, PTQ n_bits=6 (reference "
                      "quantizer graph), 6-bit inputs",
                      "encrypted_mlp_samples_per_second", "strong",
-                     cpu_baseline=program_cpu_baseline)
+                     cpu_baseline=program_cpu_baseline, comm=comm)
 
 
-def cnn_leg(args, pnb, world, rank, local, dist, dev):
+def cnn_leg(args, pnb, world, rank, local, dist, dev, comm=None):
     """Encrypted small CNN (Conv 3x3x8 s1 -> ReLU -> avg pool 2x2 -> Conv 3x3x16 s2 -> ReLU ->
     Linear 576->10; the reference quantizer's graph) on `--cnn-batch` samples per GPU (weak
     scaling: 8 GPUs evaluate the configuration's 512-sample batch)."""
@@ -659,7 +660,7 @@ def cnn_leg(args, pnb, world, rank, local, dist, dev):
                      SEED + 300,
                      "CNN 1x28x28: Conv 3x3x8 s1, ReLU, avg pool 2x2, Conv 3x3x16 s2, ReLU, "
                      "Linear 576->10 (reference quantizer graph, n_bits=6), 6-bit inputs",
-                     "encrypted_cnn_samples_per_second", "weak")
+                     "encrypted_cnn_samples_per_second", "weak", comm=comm)
 
 
 def linear_requant_graph():
@@ -677,14 +678,14 @@ def linear_requant_graph():
             "outputs": ["y"], "nodes": nodes}
 
 
-def linear_requant_leg(args, pnb, world, rank, local, dist, dev):
+def linear_requant_leg(args, pnb, world, rank, local, dist, dev, comm=None):
     """The Linear 784 -> 128 + Requant configuration end to end (contraction + bootstraps)."""
     return graph_leg(args, pnb, world, rank, local, dist, dev, linear_requant_graph(),
                      args.lr_batch * world, SEED + 200,
                      "Linear 784->128 (int4 weights U[-8,7]) + ReLU-Requant to 2 bits, 6-bit "
                      "inputs, N=2048 parameter set",
                      "encrypted_linear_requant_samples_per_second", "weak",
-                     cpu_baseline=program_cpu_baseline)
+                     cpu_baseline=program_cpu_baseline, comm=comm)
 
 
 def run_gpu(args):
@@ -700,6 +701,8 @@ def run_gpu(args):
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=dev)
     pnb = load_package()
+    # the library's own communicator carries every output all-gather (pnb_allgather over NCCL)
+    comm = pnb.Comm.from_process_group(local) if dist is not None else None
     B = args.batch
     keys = pnb.keygen(seed=SEED, device=local)  # identical replica on every rank
     rng = np.random.default_rng(SEED + rank)
@@ -727,12 +730,12 @@ def run_gpu(args):
     decrypt_ok = bool(np.array_equal(dec, lut[msgs]))
 
     # With N > 1 ranks each step is one sharded layer of bootstraps: every rank bootstraps its
-    # own 4096 ciphertexts, then one NCCL all-gather reassembles the layer's outputs on every
-    # rank (the exchange step of the sample-sharded evaluation).
+    # own 4096 ciphertexts, then one all-gather (pnb_allgather) reassembles the layer's outputs
+    # on every rank (the exchange step of the sample-sharded evaluation).
     gathered = (torch.empty((world * B, keys.big_dim + 1), dtype=torch.int64, device=dev)
                 if dist is not None else None)
-    if dist is not None:
-        dist.all_gather_into_tensor(gathered, out)  # warm the communicator
+    if comm is not None:
+        comm.allgather(out, world * B, out=gathered)  # warm the communicator
 
     # timed region: K steps, L2 flushed between steps (outside the step events)
     ev = [tuple(torch.cuda.Event(enable_timing=True) for _ in range(4))
@@ -747,8 +750,8 @@ def run_gpu(args):
             e1.record(stream)
             pnb.blind_rotate(keys, tv, small, out=out)
             e2.record(stream)
-            if dist is not None:
-                dist.all_gather_into_tensor(gathered, out)
+            if comm is not None:
+                comm.allgather(out, world * B, out=gathered)
             e3.record(stream)
         barrier()
     step_ms = [a.elapsed_time(d) for a, b, c, d in ev]
@@ -829,12 +832,14 @@ def run_gpu(args):
              if (rank == 0 and args.noise) else None)
     sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
     key_sets = key_set_leg(pnb, dev, flush) if (rank == 0 and args.key_sets) else None
-    n8k = (n8192_leg(args, pnb, world, rank, local, dist, dev, flush)
+    n8k = (n8192_leg(args, pnb, world, rank, local, dist, dev, flush, comm)
            if args.n8k else None)
     lin_rq = (None if args.lr_batch <= 0
-              else linear_requant_leg(args, pnb, world, rank, local, dist, dev))
-    cnn = None if args.cnn_batch <= 0 else cnn_leg(args, pnb, world, rank, local, dist, dev)
-    mlp = None if args.mlp_batch <= 0 else mlp_leg(args, pnb, world, rank, local, dist, dev)
+              else linear_requant_leg(args, pnb, world, rank, local, dist, dev, comm))
+    cnn = (None if args.cnn_batch <= 0
+           else cnn_leg(args, pnb, world, rank, local, dist, dev, comm))
+    mlp = (None if args.mlp_batch <= 0
+           else mlp_leg(args, pnb, world, rank, local, dist, dev, comm))
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -875,6 +880,9 @@ def run_gpu(args):
             "mlp": mlp,
         }
         print(json.dumps(line), flush=True)
+    if comm is not None:
+        torch.cuda.synchronize(dev)
+        comm.close()
     if dist is not None:
         dist.destroy_process_group()
     return 0

@@ -420,6 +420,34 @@ int pnb_add_batch(const pnb_keyring* ring, const pnb_tensor_desc* a, const uint6
                   double out_log2_sigma, uint64_t* out_dev, pnb_tensor_desc* out_desc,
                   void* stream);
 
+/* ---- sample sharding across GPUs (one process per GPU) -------------------------------------
+ * A batch is split into contiguous shards, rank r holding rows [start, stop) as pnb_shard
+ * computes (sizes differ by at most one); every GPU evaluates its shard with its own key replica
+ * (keys generated from the same seed are identical), then pnb_allgather reassembles the output
+ * rows on every rank.  NCCL is opened at run time (libnccl.so.2; a process that already loaded
+ * NCCL shares that copy) -- PNB_ERR_UNSUPPORTED when it cannot be.  The reference evaluates one
+ * sample in one process (runtime/src/eval.rs:86-166) and has no collective; this is the
+ * exchange step batching across GPUs adds. */
+typedef struct pnb_comm pnb_comm;
+#define PNB_COMM_ID_BYTES 128
+int pnb_shard(int64_t batch, int world, int rank, int64_t* start, int64_t* stop);
+/* One rank draws the id and hands its 128 bytes to the others out of band. */
+int pnb_comm_unique_id(void* id_out);
+/* Collective over `world` ranks: every rank calls it with the same id (blocking). */
+int pnb_comm_create(int device, int world, int rank, const void* id, pnb_comm** out);
+int pnb_comm_free(pnb_comm* comm);
+/* Tears the communicator down without waiting for peers (after a peer failed). */
+int pnb_comm_abort(pnb_comm* comm);
+int pnb_comm_info(const pnb_comm* comm, int* device, int* world, int* rank);
+/* PNB_OK, or the asynchronous NCCL error a collective hit (e.g. a peer that left). */
+int pnb_comm_status(const pnb_comm* comm);
+/* local_dev [stop - start][row_words] (this rank's shard of `batch` rows) -> out_dev
+ * [batch][row_words] on every rank, enqueued on `stream`: one ncclAllGather for equal shards,
+ * one grouped ncclBroadcast per rank into place for ragged ones.  local_dev may alias
+ * out_dev + start * row_words. */
+int pnb_allgather(pnb_comm* comm, const uint64_t* local_dev, uint64_t* out_dev, int64_t batch,
+                  int64_t row_words, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

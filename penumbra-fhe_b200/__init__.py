@@ -11,6 +11,7 @@ per-op kernels that replace tfhe-rs calls inside ``Linear``/``Conv2d``/``Requant
 from __future__ import annotations
 
 import ctypes as C
+import math
 import os
 
 import torch
@@ -153,6 +154,18 @@ _SIGS = {
                                    C.c_int, C.c_double, C.c_void_p, C.c_void_p, C.c_void_p]),
     "pnb_add_batch": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
                                 C.c_int, C.c_int, C.c_double, C.c_void_p, C.c_void_p,
+                                C.c_void_p]),
+    "pnb_shard": (C.c_int, [C.c_int64, C.c_int, C.c_int, C.POINTER(C.c_int64),
+                            C.POINTER(C.c_int64)]),
+    "pnb_comm_unique_id": (C.c_int, [C.c_void_p]),
+    "pnb_comm_create": (C.c_int, [C.c_int, C.c_int, C.c_int, C.c_void_p,
+                                  C.POINTER(C.c_void_p)]),
+    "pnb_comm_free": (C.c_int, [C.c_void_p]),
+    "pnb_comm_abort": (C.c_int, [C.c_void_p]),
+    "pnb_comm_info": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int),
+                                C.POINTER(C.c_int)]),
+    "pnb_comm_status": (C.c_int, [C.c_void_p]),
+    "pnb_allgather": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int64,
                                 C.c_void_p]),
 }
 
@@ -836,10 +849,93 @@ def shard(batch: int, world: int, rank: int) -> tuple[int, int]:
     return start, start + base + (1 if rank < extra else 0)
 
 
-def gather_shards(local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
+class Comm:
+    """The library's NCCL communicator (``pnb_comm``) for the output all-gather of
+    sample-sharded evaluation.  Every rank creates one with the same 128-byte id: draw it on one
+    rank with ``Comm.unique_id()`` and hand it over out of band, or let ``from_process_group``
+    broadcast it through an initialised ``torch.distributed`` group.  Close it explicitly
+    (``close``, or ``abort`` after a peer failed); it is also a context manager."""
+
+    def __init__(self, device: int, world: int, rank: int, uid: bytes):
+        if len(uid) != 128:
+            raise ValueError("a communicator id is 128 bytes")
+        buf = C.create_string_buffer(bytes(uid), 128)
+        h = C.c_void_p()
+        _check("pnb_comm_create", lib().pnb_comm_create(int(device), int(world), int(rank),
+                                                        buf, C.byref(h)))
+        self.handle, self.device, self.world, self.rank = h, int(device), int(world), int(rank)
+
+    @staticmethod
+    def unique_id() -> bytes:
+        buf = C.create_string_buffer(128)
+        _check("pnb_comm_unique_id", lib().pnb_comm_unique_id(buf))
+        return buf.raw
+
+    @classmethod
+    def from_process_group(cls, device: int, group=None) -> "Comm":
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
+        box = [cls.unique_id() if rank == 0 else None]
+        dist.broadcast_object_list(box, src=dist.get_global_rank(group, 0) if group else 0,
+                                   group=group)
+        return cls(device, world, rank, box[0])
+
+    def status(self):
+        """Raise LibraryError if a collective of this communicator hit an asynchronous error."""
+        _check("pnb_comm_status", lib().pnb_comm_status(self.handle))
+
+    def allgather(self, local: torch.Tensor, batch: int,
+                  out: torch.Tensor | None = None) -> torch.Tensor:
+        """This rank's shard ``local`` (rows ``shard(batch, world, rank)``, any trailing shape)
+        -> the full ``batch`` rows on every rank, enqueued on the current stream."""
+        a, b = shard(batch, self.world, self.rank)
+        if local.shape[0] != b - a:
+            raise ValueError(f"rank {self.rank} holds {local.shape[0]} rows, its shard is {b - a}")
+        row = tuple(local.shape[1:])
+        row_bytes = math.prod(row) * local.element_size()
+        if row_bytes == 0 or row_bytes % 8:
+            raise ValueError("rows must be a whole, non-zero number of 64-bit words")
+        if out is None:
+            out = torch.empty((batch,) + row, dtype=local.dtype, device=local.device)
+        local = local.contiguous()
+        dev = torch.device("cuda", self.device)
+        _check("pnb_allgather", lib().pnb_allgather(self.handle, _ptr(local if b > a else None),
+                                                    _ptr(out), batch, row_bytes // 8,
+                                                    _stream(dev)))
+        return out
+
+    def close(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check("pnb_comm_free", lib().pnb_comm_free(h))
+
+    def abort(self):
+        if self.handle:
+            h, self.handle = self.handle, None
+            _check("pnb_comm_abort", lib().pnb_comm_abort(h))
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+def shard_native(batch: int, world: int, rank: int) -> tuple[int, int]:
+    """``shard`` as the library computes it (``pnb_shard``)."""
+    a, b = C.c_int64(), C.c_int64()
+    _check("pnb_shard", lib().pnb_shard(batch, world, rank, C.byref(a), C.byref(b)))
+    return a.value, b.value
+
+
+def gather_shards(local: torch.Tensor, batch: int, group=None,
+                  comm: Comm | None = None) -> torch.Tensor:
     """All-gather per-rank shards (dim 0 = samples of ``shard(batch, world, rank)``) into the
-    full batch on every rank.  Shards are padded to the largest size for the collective (NCCL
-    on GPU tensors, gloo on CPU tensors) and trimmed afterwards."""
+    full batch on every rank.  With ``comm`` the library's own collective runs
+    (``pnb_allgather``); otherwise ``torch.distributed`` does, the shards padded to the
+    largest size (NCCL on GPU tensors, gloo on CPU tensors) and trimmed afterwards."""
+    if comm is not None:
+        return comm.allgather(local, batch)
     import torch.distributed as dist
     world = dist.get_world_size(group)
     sizes = [shard(batch, world, r) for r in range(world)]
@@ -856,16 +952,21 @@ def gather_shards(local: torch.Tensor, batch: int, group=None) -> torch.Tensor:
     return torch.cat(parts)
 
 
-def evaluate_sharded(ev: "Evaluator", ct_all: torch.Tensor, group=None) -> torch.Tensor:
+def evaluate_sharded(ev: "Evaluator", ct_all: torch.Tensor, group=None,
+                     comm: Comm | None = None) -> torch.Tensor:
     """Strong-scaled evaluation: every rank evaluates its contiguous shard of the batch
     ``ct_all`` [batch][input_elems][kN+1] on its own GPU (identical key replicas from the same
-    seed), then one all-gather reassembles the output ciphertexts on every rank."""
-    import torch.distributed as dist
-    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    seed), then one all-gather (the library's, given ``comm``) reassembles the output
+    ciphertexts on every rank."""
+    if comm is not None:
+        world, rank = comm.world, comm.rank
+    else:
+        import torch.distributed as dist
+        world, rank = dist.get_world_size(group), dist.get_rank(group)
     a, b = shard(ct_all.shape[0], world, rank)
     local = ev.evaluate(ct_all[a:b].contiguous()) if b > a else torch.empty(
         (0, ev.plan.output_elems, ev.row), dtype=torch.int64, device=ct_all.device)
-    return gather_shards(local, ct_all.shape[0], group)
+    return gather_shards(local, ct_all.shape[0], group, comm)
 
 
 # ---- one op at a time ----------------------------------------------------------------------

@@ -65,3 +65,24 @@ def test_shard_bounds():
             assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
             sizes = [b - a for a, b in spans]
             assert max(sizes) - min(sizes) <= 1
+
+
+def test_native_shard_matches_host_shard():
+    # pnb_shard (the C ABI's shard rule, host-only code) agrees with the Python helper and
+    # rejects out-of-range ranks.
+    pnb = load_package()
+    for batch in (0, 1, 7, 1024, 10**9 + 7):
+        for world in (1, 2, 3, 8):
+            for r in range(world):
+                assert pnb.shard_native(batch, world, r) == pnb.shard(batch, world, r)
+    with pytest.raises(pnb.LibraryError):
+        pnb.shard_native(8, 2, 2)
+    with pytest.raises(pnb.LibraryError):
+        pnb.shard_native(-1, 2, 0)
+
+
+def test_comm_id_is_drawn_without_a_gpu():
+    # The communicator id is a host-side bootstrap address: drawing one needs no device.
+    pnb = load_package()
+    a, b = pnb.Comm.unique_id(), pnb.Comm.unique_id()
+    assert len(a) == 128 and a != b
