@@ -25,11 +25,13 @@ namespace pnb {
 __device__ int g_br_status;
 
 int br_status_read_and_clear(int* out) {
-  int v = 0;
+  int v = 0, v8 = 0;
   PNB_CUDA(cudaMemcpyFromSymbol(&v, g_br_status, sizeof(int)));
   const int zero = 0;
   PNB_CUDA(cudaMemcpyToSymbol(g_br_status, &zero, sizeof(int)));
-  *out = v;
+  const int rc = br8_status_read_and_clear(&v8);  // the N = 8192 rotation's word
+  if (rc) return rc;
+  *out = v | v8;
   return PNB_OK;
 }
 

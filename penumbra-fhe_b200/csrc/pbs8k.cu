@@ -21,8 +21,12 @@
 // Rotation: one ciphertext per block of 256 threads.  The accumulator (top 32 bits of each torus
 // coefficient, coefficients j and j + M side by side) sits in shared memory with one 64 KB
 // transpose buffer; per CMux every (row, level) digit polynomial is transformed and multiplied
-// into both output spectra, which stay in registers until their inverse transforms.  The key is
-// read from L2: one GGSW level of 256 KB per CMux does not fit shared memory.
+// into both output spectra, which stay in registers until their inverse transforms.  One GGSW
+// row (two output polynomials, 128 KB) does not fit shared memory beside the transpose buffer and
+// the accumulator, so the key streams through a ring of 32 KB stages filled by bulk copies
+// (cp.async.bulk, no multicast) one step ahead of the products: while a row's digits are formed
+// and transformed, the first stages of its key land.  The transform's twiddle tables sit in
+// tensor memory (each warp's threads' factors in its lane quarter), not behind L1.
 #include <cmath>
 #include <mutex>
 #include <vector>
@@ -36,6 +40,18 @@ namespace pnb {
 
 constexpr int N8 = 8192, M8 = 4096, T8 = 256;  // polynomial size, points, threads
 constexpr int BR8_MAXN = 1024;                  // small LWE dimension the shared layout holds
+
+// Device-side status word of the N = 8192 rotation: non-zero when a bounded wait ran out.
+__device__ int g_br8_status;
+
+int br8_status_read_and_clear(int* out) {
+  int v = 0;
+  PNB_CUDA(cudaMemcpyFromSymbol(&v, g_br8_status, sizeof(int)));
+  const int zero = 0;
+  PNB_CUDA(cudaMemcpyToSymbol(g_br8_status, &zero, sizeof(int)));
+  *out = v;
+  return PNB_OK;
+}
 
 // ---- tables (one set per device) -----------------------------------------------------------
 struct Fft8Tables {
@@ -176,6 +192,102 @@ __device__ __forceinline__ void inv8k(double2 (&x)[16], double2* buf, const Fft8
   }
 }
 
+// The rotation's transforms take the twiddle factors of this thread from tensor memory: per
+// warp, columns [0, 64) hold tw1[k1][t] for k1 = 0..15 and [64, 128) hold tw2[k3][t & 15] for
+// k3 = 0..15, each complex value as four 32-bit words (re lo, re hi, im lo, im hi).
+__device__ __forceinline__ void tw_words(double2 v, uint32_t* w) {
+  w[0] = (uint32_t)__double2loint(v.x);
+  w[1] = (uint32_t)__double2hiint(v.x);
+  w[2] = (uint32_t)__double2loint(v.y);
+  w[3] = (uint32_t)__double2hiint(v.y);
+}
+
+// x[q] *= T[q] (CONJ: by conj(T[q])) for the 16 factors at tensor-memory address `ta`.
+#ifndef PNB_BR8_TW_CHUNK
+#define PNB_BR8_TW_CHUNK 4  // complex factors per tensor-memory load (4: 16 columns, 8: 32)
+#endif
+__device__ __forceinline__ void tm_words(uint32_t ta, uint32_t (&w)[16]) {
+  tc::tmem_ld_32x32_x16(ta, w);
+}
+__device__ __forceinline__ void tm_words(uint32_t ta, uint32_t (&w)[32]) {
+  tc::tmem_ld_32x32_nowait(ta, w);
+}
+template <bool CONJ>
+__device__ __forceinline__ void tm_twiddle16(double2 (&x)[16], uint32_t ta) {
+  constexpr int C = PNB_BR8_TW_CHUNK;
+  static_assert(C == 4 || C == 8, "4 or 8 factors per load");
+#pragma unroll
+  for (int g = 0; g < 16 / C; ++g) {
+    uint32_t w[4 * C];
+    tm_words(ta + 4u * C * g, w);
+    tc::tmem_ld_wait();
+#pragma unroll
+    for (int q = 0; q < C; ++q) {
+      const double2 c = make_double2(__hiloint2double((int)w[4 * q + 1], (int)w[4 * q]),
+                                     __hiloint2double((int)w[4 * q + 3], (int)w[4 * q + 2]));
+      x[C * g + q] = CONJ ? cmul_conj(x[C * g + q], c) : cmul(x[C * g + q], c);
+    }
+  }
+}
+
+// fwd8k with the twiddles from tensor memory (t_tw1, t_tw2: this warp's column bases).
+__device__ __forceinline__ void fwd8k_tm(double2 (&x)[16], double2* buf, const Fft8Tables& tb,
+                                         uint32_t t_tw1, uint32_t t_tw2) {
+  const int t = threadIdx.x;
+#pragma unroll
+  for (int m = 0; m < 16; ++m) x[m] = cmul(x[m], __ldg(&tb.cm[m]));
+  dft16<1>(x);
+  tm_twiddle16<false>(x, t_tw1);
+#pragma unroll
+  for (int k1 = 0; k1 < 16; ++k1) buf[swz8(t, k1)] = x[k1];
+  __syncthreads();
+  const int k1 = t >> 4, j4 = t & 15;
+#pragma unroll
+  for (int j3 = 0; j3 < 16; ++j3) x[j3] = buf[swz8(16 * j3 + j4, k1)];
+  __syncthreads();
+  dft16<1>(x);
+  tm_twiddle16<false>(x, t_tw2);
+#pragma unroll
+  for (int k3 = 0; k3 < 16; ++k3) buf[swz8(16 * k1 + j4, k3)] = x[k3];
+  __syncthreads();
+  const int k3 = t & 15;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) x[q] = buf[swz8(16 * k1 + q, k3)];
+  __syncthreads();
+  dft16<1>(x);
+}
+
+// inv8k with the twiddles from tensor memory.
+__device__ __forceinline__ void inv8k_tm(double2 (&x)[16], double2* buf, const Fft8Tables& tb,
+                                         uint32_t t_tw1, uint32_t t_tw2, double scale) {
+  const int t = threadIdx.x;
+  const int k1 = t >> 4, k3 = t & 15;
+  dft16<-1>(x);
+#pragma unroll
+  for (int j4 = 0; j4 < 16; ++j4) buf[swz8(16 * k1 + j4, k3)] = x[j4];
+  __syncthreads();
+  const int j4 = t & 15;
+#pragma unroll
+  for (int q = 0; q < 16; ++q) x[q] = buf[swz8(16 * k1 + j4, q)];
+  __syncthreads();
+  tm_twiddle16<true>(x, t_tw2);
+  dft16<-1>(x);
+#pragma unroll
+  for (int j3 = 0; j3 < 16; ++j3) buf[swz8(16 * j3 + j4, k1)] = x[j3];
+  __syncthreads();
+#pragma unroll
+  for (int q = 0; q < 16; ++q) x[q] = buf[swz8(t, q)];
+  __syncthreads();
+  tm_twiddle16<true>(x, t_tw1);
+  dft16<-1>(x);
+  const double sc = scale * (1.0 / 4096.0);
+#pragma unroll
+  for (int m = 0; m < 16; ++m) {
+    const double2 c = __ldg(&tb.cm[m]);
+    x[m] = cmul(x[m], make_double2(c.x * sc, -c.y * sc));
+  }
+}
+
 // ---- Fourier conversion of the bootstrapping key ------------------------------------------
 __global__ void __launch_bounds__(T8) bsk8k_to_fourier_kernel(const uint64_t* __restrict__ bsk,
                                                               double2* __restrict__ fbsk,
@@ -255,16 +367,26 @@ int fft_negacyclic_mul_8k(const int64_t* a, const uint64_t* b, uint64_t* out, in
 }
 
 // ---- blind rotation ----------------------------------------------------------------------------
+template <bool W48>
 struct Br8Layout {
-  static constexpr int BUF = M8 * sizeof(double2);        // 64 KB transpose buffer
-  static constexpr int ACC = 2 * M8 * sizeof(uint2);      // 64 KB: bits 32..63, pairs
-  static constexpr int LO = 2 * M8 * sizeof(ushort2);     // 32 KB: bits 16..31 (48-bit form)
+  static constexpr int BUF = M8 * sizeof(double2);                // 64 KB transpose buffer
+  static constexpr int ACC = 2 * M8 * sizeof(uint2);              // 64 KB: bits 32..63, pairs
+  static constexpr int LO = W48 ? 2 * M8 * sizeof(ushort2) : 0;   // 32 KB: bits 16..31
+  static constexpr int STAGE = 2 * 4 * T8 * sizeof(double2);      // 32 KB: 4 spectral registers
+  static constexpr int STAGES = W48 ? 2 : 3;                      //   of both output polynomials
   static constexpr int ABAR = BR8_MAXN * sizeof(uint16_t);
   static constexpr int OFF_ACC = BUF;
   static constexpr int OFF_LO = OFF_ACC + ACC;
-  static constexpr int OFF_ABAR = OFF_LO + LO;
-  static constexpr int BYTES = OFF_ABAR + ABAR;
+  static constexpr int OFF_RING = OFF_LO + LO;
+  static constexpr int OFF_ABAR = OFF_RING + STAGES * STAGE;
+  static constexpr int OFF_BAR = OFF_ABAR + ABAR;  // full[3], empty[3], abort flag, TMEM base
+  static constexpr int BYTES = OFF_BAR + 64;
+  static constexpr int TMEM_COLS = 256;  // per warp 128: tw1 and tw2 factors
 };
+static_assert(Br8Layout<false>::BYTES <= 227 * 1024 && Br8Layout<true>::BYTES <= 227 * 1024,
+              "the N = 8192 rotation's shared layout exceeds 227 KB");
+
+constexpr uint32_t BR8_WAIT_LIMIT = 1u << 24;
 
 // The 48-bit form: w = v 2^-16; round(w) mod 2^48 in the top 48 bits of a torus word (pbs.cu's
 // construction with 2^48 in place of 2^32).
@@ -300,16 +422,71 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
     Fft8Tables tb) {
   constexpr bool W48 = BETA * L > 30;
   static_assert(BETA * L <= 46, "the 48-bit accumulator holds the digits and a rounding bit");
-  using Y = Br8Layout;
+  using Y = Br8Layout<W48>;
+  constexpr int S = Y::STAGES;
   extern __shared__ __align__(128) unsigned char b8_raw[];
   double2* buf = reinterpret_cast<double2*>(b8_raw);
   uint2* acc = reinterpret_cast<uint2*>(b8_raw + Y::OFF_ACC);  // [poly][pair j]
   ushort2* lo = reinterpret_cast<ushort2*>(b8_raw + Y::OFF_LO); // [poly][pair j], 48-bit form
+  const double2* ring = reinterpret_cast<const double2*>(b8_raw + Y::OFF_RING);
   uint16_t* abar = reinterpret_cast<uint16_t*>(b8_raw + Y::OFF_ABAR);
-  const int t = threadIdx.x;
+  const uint32_t full0 = tc::smem_u32(b8_raw + Y::OFF_BAR);  // full[s] at +8 s
+  const uint32_t empty0 = full0 + 24;                         // empty[s] at +24 + 8 s
+  volatile int* abort_s = reinterpret_cast<volatile int*>(b8_raw + Y::OFF_BAR + 48);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(b8_raw + Y::OFF_BAR + 52);
+  const uint32_t ring_u32 = tc::smem_u32(b8_raw + Y::OFF_RING);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
   const int ct = blockIdx.x;
   if (ct >= count) return;
   constexpr int LG = 14;  // log2(2N)
+
+  // The key streams in chunks g = (i (2L) + row) 4 + c: spectral registers 4c..4c+3 of both
+  // output polynomials of GGSW i, row `row` (two contiguous 16 KB pieces), into stage g mod S.
+  const int total = n * (2 * L) * 4;  // <= 2^15 chunks
+  auto issue = [&](int g) {
+    const int st = g % S;
+    const double2* f = fbsk + (size_t)(g >> 2) * 2 * M8 + (size_t)(g & 3) * 4 * T8;
+    const uint32_t dst = ring_u32 + (uint32_t)st * Y::STAGE;
+    tc::mbar_expect_tx(full0 + 8u * st, Y::STAGE);
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      asm volatile(
+          "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, "
+          "[%3];" ::"r"(dst + (uint32_t)h * (Y::STAGE / 2)), "l"(f + (size_t)h * M8),
+          "r"(Y::STAGE / 2), "r"(full0 + 8u * st)
+          : "memory");
+  };
+  if (t == 0) {
+    for (int st = 0; st < S; ++st) {
+      tc::mbar_init(full0 + 8u * st, 1);
+      tc::mbar_init(empty0 + 8u * st, T8 / 32);
+    }
+    tc::fence_mbar_init();
+    *abort_s = 0;
+  }
+  if (warp == 0) tc::tmem_alloc(tc::smem_u32(tmem_holder), Y::TMEM_COLS);
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  if (t == 0)
+    for (int g = 0; g < S && g < total; ++g) issue(g);
+  int issued = total < S ? total : S;  // thread 0's count
+  // this warp's twiddle factors: lane quarter warp & 3, columns 128 (warp >> 2) + [0, 128)
+  const uint32_t t_tw1 = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
+                         ((uint32_t)(32 * (warp & 3)) << 16) + 128u * (uint32_t)(warp >> 2);
+  const uint32_t t_tw2 = t_tw1 + 64u;
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {
+    uint32_t a[16], b[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      tw_words(tb.tw1[(4 * g + q) * T8 + t], a + 4 * q);
+      tw_words(tb.tw2[(4 * g + q) * 16 + (t & 15)], b + 4 * q);
+    }
+    tc::tmem_st_32x32_x16(t_tw1 + 16u * g, a);
+    tc::tmem_st_32x32_x16(t_tw2 + 16u * g, b);
+  }
+  tc::tmem_st_wait();
   const uint64_t* in = small_ct + (size_t)ct * (n + 1);
   const uint64_t* tv =
       tv_idx ? tvs + (size_t)tv_idx[(int)(((long long)tv_first + ct) % tv_period)] * N8 : tvs;
@@ -369,7 +546,7 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
         const uint2 g = ap[tr & (M8 - 1)], own = ap[j];
         const bool sw = (unsigned)(tr + M8) < (unsigned)M8;
         int d0, d1;
-        if (!W48) {
+        if constexpr (!W48) {
           const int sh = 32 - BETA * (lev + 1);
           const uint32_t w0 = (tr < 0) ? ~flip0 : flip0, w1 = (tr < -M8) ? ~flip0 : flip0;
           const uint32_t g0 = sw ? g.y : g.x, g1 = sw ? g.x : g.y;
@@ -396,15 +573,40 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
         }
         x[m] = make_double2((double)d0, (double)d1);
       }
-      fwd8k(x, buf, tb);
-      // GGSW i, row (p, lev): its two output polynomials in the spectral distribution
-      const double2* f = fbsk + ((size_t)i * (2 * L) + row) * 2 * M8;
+      fwd8k_tm(x, buf, tb, t_tw1, t_tw2);
+      // GGSW i, row (p, lev): its two output polynomials in the spectral distribution, four
+      // registers per ring stage
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const double2 f0 = __ldg(&f[q * T8 + v]), f1 = __ldg(&f[M8 + q * T8 + v]);
-        const double2 a0 = cmul(x[q], f0), a1 = cmul(x[q], f1);
-        o0[q].x += a0.x; o0[q].y += a0.y;
-        o1[q].x += a1.x; o1[q].y += a1.y;
+      for (int c = 0; c < 4; ++c) {
+        const int g = (i * (2 * L) + row) * 4 + c;
+        const int st = g % S;
+        const uint32_t ph = (uint32_t)((g / S) & 1);
+        if (!*abort_s && !tc::mbar_wait(full0 + 8u * st, ph, BR8_WAIT_LIMIT)) {
+          *abort_s = 1;
+          atomicExch(&g_br8_status, 1);
+        }
+        const double2* f = ring + (size_t)st * (Y::STAGE / sizeof(double2));
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int q = 4 * c + q4;
+          const double2 f0 = f[q4 * T8 + v], f1 = f[4 * T8 + q4 * T8 + v];
+          const double2 a0 = cmul(x[q], f0), a1 = cmul(x[q], f1);
+          o0[q].x += a0.x; o0[q].y += a0.y;
+          o1[q].x += a1.x; o1[q].y += a1.y;
+        }
+        __syncwarp();
+        if (lane == 0) tc::mbar_arrive(empty0 + 8u * st);
+        // stage st is free once every warp has read it: refill it S chunks ahead
+        if (t == 0 && g + S < total && !*abort_s) {
+          if (!tc::mbar_wait(empty0 + 8u * st, ph, BR8_WAIT_LIMIT)) {
+            *abort_s = 1;
+            atomicExch(&g_br8_status, 1);
+          } else {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(g + S);
+            ++issued;
+          }
+        }
       }
     }
     // both output polynomials back to coefficients; every thread has read the accumulator
@@ -414,7 +616,7 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
       double2 x[16];
 #pragma unroll
       for (int q = 0; q < 16; ++q) x[q] = p == 0 ? o0[q] : o1[q];
-      inv8k(x, buf, tb, W48 ? 0x1p-16 : 0x1p-32);
+      inv8k_tm(x, buf, tb, t_tw1, t_tw2, W48 ? 0x1p-16 : 0x1p-32);
       uint2* ap = acc + p * M8;
       ushort2* lp = lo + p * M8;
 #pragma unroll
@@ -435,7 +637,20 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
       }
     }
     __syncthreads();
+    if (*abort_s) break;  // uniform: every thread reads the flag after the same barrier
   }
+  // the copies still in flight (only after a wait gave up) land before the block exits
+  if (t == 0 && *abort_s)
+    for (int g = issued - S < 0 ? 0 : issued - S; g < issued; ++g)
+      (void)tc::mbar_wait(full0 + 8u * (uint32_t)(g % S), (uint32_t)((g / S) & 1),
+                          BR8_WAIT_LIMIT);
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(*reinterpret_cast<volatile uint32_t*>(tmem_holder), Y::TMEM_COLS);
+  }
+  if (*abort_s) return;
   // sample extraction of coefficient 0 under the big key
   uint64_t* o = out + (size_t)ct * out_ld;
   auto coef = [&](int p, int e) {
@@ -458,7 +673,7 @@ static int launch8k(const pnb_keys* K, const uint64_t* tvs, const int32_t* tv_id
   Fft8Tables tb;
   int rc = fft8_tables_get(&tb);
   if (rc) return rc;
-  constexpr int smem = Br8Layout::BYTES;
+  constexpr int smem = Br8Layout<(BETA * L > 30)>::BYTES;
   PNB_CUDA(cudaFuncSetAttribute(blind_rotate8k_kernel<L, BETA>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   blind_rotate8k_kernel<L, BETA><<<count, T8, smem, st>>>(small, tvs, tv_idx, period, first,

@@ -79,5 +79,6 @@ bool fft_tables_ready();
 int pbs_batch_noalloc(const pnb_keys* K, const uint64_t* tv, const uint64_t* in, uint64_t* out,
                       int count, cudaStream_t st);
 int br_status_read_and_clear(int* out);
+int br8_status_read_and_clear(int* out);
 int ct_status_read_and_clear(int* out);
 }  // namespace pnb
