@@ -198,6 +198,24 @@ def run_reference(args):
     return 0
 
 
+def device_timed(fn, flush, steps, stream):
+    """Device time of `steps` launches of fn(), each after an L2 flush, from CUDA events around
+    each launch.  A device-side spin queued first lets the host enqueue every step before the
+    GPU reaches them, so host-side launch latency never lands inside an event pair."""
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    torch.cuda.synchronize()
+    torch.cuda._sleep(50_000_000)  # ~25 ms of GPU cycles ahead of the first step
+    for a, b in evs:
+        flush.zero_()
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
 def contraction_leg(args, pnb, local, dev, flush):
     """Encrypted Linear 784 -> 128 (int4 weights, 256 samples) on the tensor cores.
 
@@ -216,16 +234,8 @@ def contraction_leg(args, pnb, local, dev, flush):
     stream = torch.cuda.current_stream(dev)
     for _ in range(max(args.warmup, 1)):
         pnb.lwe_contract_ld(W, bias, 1 << 40, X, L, out=Y)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(args.steps)]
-    torch.cuda.synchronize(dev)
-    for a, b in evs:
-        flush.zero_()
-        a.record(stream)
-        pnb.lwe_contract_ld(W, bias, 1 << 40, X, L, out=Y)
-        b.record(stream)
-    torch.cuda.synchronize(dev)
-    ms = [a.elapsed_time(b) for a, b in evs]
+    ms = device_timed(lambda: pnb.lwe_contract_ld(W, bias, 1 << 40, X, L, out=Y), flush,
+                      args.steps, stream)
     avg = sum(ms) / len(ms)
     algo_bytes = B * K * L * 8 + B * M * L * 8 + M * K + M * 8
     peak = _measured_hbm()
@@ -293,15 +303,8 @@ def n8192_leg(args, pnb, world, rank, local, dist, dev, flush, comm=None):
     X = torch.randint(-(1 << 62), 1 << 62, (Bc, K, LD), dtype=torch.int64, device=dev)
     Y = torch.empty((Bc, M, LD), dtype=torch.int64, device=dev)
     pnb.lwe_contract_ld(Wt, bias, 1 << 40, X, L, out=Y)
-    cms = []
-    for _ in range(5):
-        flush.zero_()
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record(stream)
-        pnb.lwe_contract_ld(Wt, bias, 1 << 40, X, L, out=Y)
-        b.record(stream)
-        torch.cuda.synchronize(dev)
-        cms.append(a.elapsed_time(b))
+    cms = device_timed(lambda: pnb.lwe_contract_ld(Wt, bias, 1 << 40, X, L, out=Y), flush, 5,
+                       stream)
     del X, Y
     avg = sum(cms) / len(cms)
     algo = Bc * K * L * 8 + Bc * M * L * 8 + M * K + M * 8

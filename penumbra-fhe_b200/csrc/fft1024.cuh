@@ -116,6 +116,47 @@ __device__ __forceinline__ void crt_dft32(double2 (&x)[FFT_R]) {
   crt_stage<5, TH0, CB>(x);
 }
 
+// Butterfly of stage K (1..5) of the reduction tree of X^32 - exp(2 pi i TH0 / 128) on the pair
+// (i, i + H), H = 32 >> K, as crt_stage<K, TH0> does it.
+template <int K, int TH0, bool CB>
+__device__ __forceinline__ void crt_bfly_at(double2 (&x)[FFT_R], int i) {
+  constexpr int H = 32 >> K;
+  const int e = (TH0 + 128 * bitrev_bits(i / (2 * H), K - 1)) >> K;
+  ct_bfly<CB>(e, x[i], x[i + H]);
+}
+
+// crt_dft32<TH0> over inputs that `src(m)` produces (the value for register m), with every
+// butterfly of stages 1-4 issued as soon as its operands exist: the input pairs (r, r + 16) come
+// in 4-bit bit-reversed order of r, so after pairs r and r + 8 stage 2 can run on them, after four
+// pairs stage 3, after eight stage 4.  The integer work that forms the inputs and the FP64
+// butterflies then interleave in one instruction stream; every value meets the same butterflies
+// in the same order as in crt_dft32, so the results are identical.
+template <int TH0, bool CB, typename Src>
+__device__ __forceinline__ void crt_dft32_from(double2 (&x)[FFT_R], Src&& src) {
+#pragma unroll
+  for (int k = 0; k < 16; ++k) {
+    const int r = bitrev_bits(k, 4);
+    x[r] = src(r);
+    x[r + 16] = src(r + 16);
+    crt_bfly_at<1, TH0, CB>(x, r);
+    if (k & 1) {  // pairs r - 8 and r are in
+      crt_bfly_at<2, TH0, CB>(x, r - 8);
+      crt_bfly_at<2, TH0, CB>(x, r + 8);
+    }
+    if ((k & 3) == 3) {  // every pair of residue j mod 4 is in
+      const int j = bitrev_bits(k - 3, 4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) crt_bfly_at<3, TH0, CB>(x, 8 * q + j);
+    }
+    if ((k & 7) == 7) {  // every pair of residue j mod 2 is in
+      const int j = bitrev_bits(k - 7, 4);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) crt_bfly_at<4, TH0, CB>(x, 4 * q + j);
+    }
+  }
+  crt_stage<5, TH0, CB>(x);
+}
+
 // Decimation-in-time stage of span 2^K: twiddle exp(-2 pi i j / 2^K) on the upper element.
 template <int K, bool CB>
 __device__ __forceinline__ void dit_stage(double2 (&x)[FFT_R]) {
@@ -125,6 +166,22 @@ __device__ __forceinline__ void dit_stage(double2 (&x)[FFT_R]) {
 #pragma unroll
     for (int j = 0; j < HALF; ++j) ct_bfly<CB>(128 - j * (128 >> K), x[s + j], x[s + j + HALF]);
   }
+}
+
+// Stages 1-3 of dit_dft32 on registers 8b..8b+7 alone (those stages never mix blocks of eight),
+// so a block can be transformed as soon as its inputs exist; the butterflies are dit_stage's.
+template <bool CB>
+__device__ __forceinline__ void dit_block8(double2 (&x)[FFT_R], int b) {
+  const int s0 = 8 * b;
+#pragma unroll
+  for (int s = 0; s < 8; s += 2) ct_bfly<CB>(128, x[s0 + s], x[s0 + s + 1]);
+#pragma unroll
+  for (int s = 0; s < 8; s += 4) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) ct_bfly<CB>(128 - 32 * j, x[s0 + s + j], x[s0 + s + j + 2]);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) ct_bfly<CB>(128 - 16 * j, x[s0 + j], x[s0 + j + 4]);
 }
 
 // out_k = sum_n in_n exp(-2 pi i n k / 32) with in_n in register br(n), out_k in register k.
@@ -140,22 +197,52 @@ __device__ __forceinline__ void dit_dft32(double2 (&x)[FFT_R]) {
 // x_m *= exp(-2 pi i m / 128) * 2^-SHIFT, SHIFT = 10 (the 1/M), 26 or 42 (also the 2^-16 or
 // 2^-32 a blind rotation's rounding expects); the constants come pre-scaled.
 template <int SHIFT, bool CB>
-__device__ __forceinline__ void untwist(double2 (&x)[FFT_R]) {
+__device__ __forceinline__ void untwist_at(double2 (&x)[FFT_R], int m) {
   static_assert(SHIFT == 10 || SHIFT == 26 || SHIFT == 42, "no untwist table for this scale");
   const double2* k = SHIFT == 10 ? kUntwist10 : SHIFT == 26 ? kUntwist26 : kUntwist42;
   constexpr double sc = 1.0 / (double)(1ull << SHIFT);
+  double c, sn;
+  if (CB) {
+    c = k[m].x;
+    sn = k[m].y;
+  } else {
+    cs128_lit((128 - m) & 127, c, sn);
+    c *= sc;  // literals: folded at compile time
+    sn *= sc;
+  }
+  x[m] = m == 0 ? make_double2(x[m].x * c, x[m].y * c) : cmul(x[m], make_double2(c, sn));
+}
+
+template <int SHIFT, bool CB>
+__device__ __forceinline__ void untwist(double2 (&x)[FFT_R]) {
 #pragma unroll
-  for (int m = 0; m < 32; ++m) {
-    double c, sn;
-    if (CB) {
-      c = k[m].x;
-      sn = k[m].y;
-    } else {
-      cs128_lit((128 - m) & 127, c, sn);
-      c *= sc;  // literals: folded at compile time
-      sn *= sc;
-    }
-    x[m] = m == 0 ? make_double2(x[m].x * c, x[m].y * c) : cmul(x[m], make_double2(c, sn));
+  for (int m = 0; m < 32; ++m) untwist_at<SHIFT, CB>(x, m);
+}
+
+// dit_dft32 followed by untwist<SHIFT>, handing every finished register m to `sink(m)` as soon
+// as its last butterfly and its untwist are done: after stages 1-3, stages 4 and 5 run in eight
+// chunks (stage-4 pairs (j, j + 8) and (16 + j, 24 + j), then stage-5 pairs (j, j + 16) and
+// (j + 8, j + 24)), so the consumer's work on one chunk interleaves with the next chunk's
+// butterflies.  The arithmetic per value is that of dit_dft32 and untwist, in the same order.
+template <int SHIFT, bool CB, typename Sink>
+__device__ __forceinline__ void dit_dft32_untwist_to(double2 (&x)[FFT_R], Sink&& sink) {
+  dit_stage<1, CB>(x);
+  dit_stage<2, CB>(x);
+  dit_stage<3, CB>(x);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    ct_bfly<CB>(128 - 8 * j, x[j], x[j + 8]);
+    ct_bfly<CB>(128 - 8 * j, x[16 + j], x[24 + j]);
+    ct_bfly<CB>(128 - 4 * j, x[j], x[j + 16]);
+    ct_bfly<CB>(128 - 4 * (j + 8), x[j + 8], x[j + 24]);
+    untwist_at<SHIFT, CB>(x, j);
+    sink(j);
+    untwist_at<SHIFT, CB>(x, j + 16);
+    sink(j + 16);
+    untwist_at<SHIFT, CB>(x, j + 8);
+    sink(j + 8);
+    untwist_at<SHIFT, CB>(x, j + 24);
+    sink(j + 24);
   }
 }
 

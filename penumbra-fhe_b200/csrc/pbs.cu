@@ -437,17 +437,11 @@ __device__ __forceinline__ uint32_t top32_round(double w) {
   return scaled_f64_to_top32(w);
 #endif
 }
-
-// Complex values per tensor-memory round trip in the rotation (4: 16 columns, 8: 32 columns);
-// tcgen05.wait::ld waits for every load in flight, so a round trip is one load and one wait.
-#ifndef PNB_BR_TM_CHUNK
-#define PNB_BR_TM_CHUNK 8
-#endif
-template <int C>
-__device__ __forceinline__ void tm_load(uint32_t taddr, uint32_t (&t)[4 * C]) {
-  static_assert(C == 4 || C == 8, "4 or 8 complex values per load");
-  if constexpr (C == 4) tc::tmem_ld_32x32_x16(taddr, t);
-  else tc::tmem_ld_32x32_nowait(taddr, t);
+// Eight complex values (32 columns) per tensor-memory round trip: tcgen05.wait::ld waits for
+// every load in flight, so a round trip is one load and one wait.
+constexpr int BR_TC = 8;
+__device__ __forceinline__ void tm_load8(uint32_t taddr, uint32_t (&t)[32]) {
+  tc::tmem_ld_32x32_nowait(taddr, t);
   tc::tmem_ld_wait();
 }
 
@@ -522,14 +516,18 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
   const double2* f_own = bsk_s + (size_t)(p * 2 + p) * FFT_M;
   const double2* f_oth = bsk_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
 
+  // Each CMux interleaves integer or shared-memory work with FP64 butterflies in one instruction
+  // stream: the digit formation with the forward transform's first pass (crt_dft32_from), the
+  // products with the inverse transform's first four stages (per block of eight and per half),
+  // and the accumulator update with its last stage (dit_dft32_untwist_to).  Every value meets
+  // the same operations in the same order as in the plain transforms.
   for (int i = 0; i < n; ++i) {
     const int a = abar[i];
     const int ar = a & (FFT_N - 1);
     const uint32_t flip0 = (a >= FFT_N) ? 0xffffffffu : 0u;
     double2 x[FFT_R];
-#pragma unroll
-    for (int m = 0; m < 32; ++m) {
-      if ((m & 7) == 0) asm volatile("" ::: "memory");
+    // digits of (X^a - 1) acc for register m: coefficients lane + 32 m and lane + 32 m + M
+    auto digit_pair = [&](int m) -> double2 {
       const int j = lane + 32 * m;
       const int t = j - ar;
       const uint2 g = acc2[t & (FFT_M - 1)], own = acc2[j];
@@ -540,17 +538,17 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
       const uint32_t v1 = ((g1 ^ w1) - w1) - own.y;
       const int d0 = (int)(v0 + rnd) >> shift;
       const int d1 = (int)(v1 + rnd) >> shift;
-      x[m] = make_double2((double)d0, (double)d1);
-    }
-    // forward transform, the mid twiddles from tensor memory
-    crt_dft32<32, PNB_BR_CBANK>(x);
-    constexpr int TC = PNB_BR_TM_CHUNK;
+      return make_double2((double)d0, (double)d1);
+    };
+    crt_dft32_from<32, PNB_BR_CBANK>(x, digit_pair);
+    // the mid twiddles from tensor memory
 #pragma unroll
-    for (int g = 0; g < 32 / TC; ++g) {
-      uint32_t t[4 * TC];
-      tm_load<TC>(t_fwd + 4u * TC * g, t);
+    for (int g = 0; g < 32 / BR_TC; ++g) {
+      uint32_t t[4 * BR_TC];
+      tm_load8(t_fwd + 4u * BR_TC * g, t);
 #pragma unroll
-      for (int q = 0; q < TC; ++q) x[TC * g + q] = cmul(x[TC * g + q], words_to_d2(t + 4 * q));
+      for (int q = 0; q < BR_TC; ++q)
+        x[BR_TC * g + q] = cmul(x[BR_TC * g + q], words_to_d2(t + 4 * q));
     }
     warp_transpose_half(x, buf, lane);
     crt_dft32<0, PNB_BR_CBANK>(x);
@@ -571,14 +569,15 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
     tc::tc_fence_before();
     pair_sync(cl);
     tc::tc_fence_after();
-    // output polynomial p = D_own * F[own row][p] + D_other * F[other row][p]
+    // output polynomial p = D_own * F[own row][p] + D_other * F[other row][p], then the inverse
+    // transform's stages 1-3 per block of eight registers and stage 4 per half of sixteen
 #pragma unroll
-    for (int g = 0; g < 32 / TC; ++g) {
-      uint32_t t[4 * TC];
-      tm_load<TC>(t_oth + 4u * TC * g, t);
+    for (int g = 0; g < 32 / BR_TC; ++g) {
+      uint32_t t[4 * BR_TC];
+      tm_load8(t_oth + 4u * BR_TC * g, t);
 #pragma unroll
-      for (int q = 0; q < TC; ++q) {
-        const int r = TC * g + q;
+      for (int q = 0; q < BR_TC; ++q) {
+        const int r = BR_TC * g + q;
         const int e = r * 32 + lane;
         const double2 fo = f_own[e], ft = f_oth[e];
         const double2 dt = words_to_d2(t + 4 * q);
@@ -586,6 +585,12 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
         const double2 xv = x[r];
         x[r] = make_double2(fma(xv.x, fo.x, fma(-xv.y, fo.y, fma(dt.x, ft.x, -dt.y * ft.y))),
                             fma(xv.x, fo.y, fma(xv.y, fo.x, fma(dt.x, ft.y, dt.y * ft.x))));
+      }
+      dit_block8<PNB_BR_CBANK>(x, g);
+      if (g & 1) {  // dit_stage<4> on registers 16 (g >> 1) .. + 15
+        const int s0 = 16 * (g >> 1);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) ct_bfly<PNB_BR_CBANK>(128 - 8 * j, x[s0 + j], x[s0 + j + 8]);
       }
     }
     // Every warp is done with GGSW i and with the other warp's spectrum: stage GGSW i+1 while
@@ -601,28 +606,25 @@ __global__ void __launch_bounds__(64 * CPB, 1) blind_rotate_tm_kernel(
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       br_stage_ggsw(bsk_dst, fbsk + (size_t)(i + 1) * 4 * FFT_M, bar);
     }
-    // inverse transform, the conjugate twiddles from tensor memory
-    dit_dft32<PNB_BR_CBANK>(x);
+    // inverse transform: its last first-pass stage, the conjugate twiddles from tensor memory
+    dit_stage<5, PNB_BR_CBANK>(x);
 #pragma unroll
-    for (int g = 0; g < 32 / TC; ++g) {
-      uint32_t t[4 * TC];
-      tm_load<TC>(t_inv + 4u * TC * g, t);
+    for (int g = 0; g < 32 / BR_TC; ++g) {
+      uint32_t t[4 * BR_TC];
+      tm_load8(t_inv + 4u * BR_TC * g, t);
 #pragma unroll
-      for (int q = 0; q < TC; ++q)
-        x[TC * g + q] = cmul_conj(x[TC * g + q], words_to_d2(t + 4 * q));
+      for (int q = 0; q < BR_TC; ++q)
+        x[BR_TC * g + q] = cmul_conj(x[BR_TC * g + q], words_to_d2(t + 4 * q));
     }
     warp_transpose_half(x, buf, lane);
-    dit_dft32<PNB_BR_CBANK>(x);
-    untwist<10 + 32, PNB_BR_CBANK>(x);
-#pragma unroll
-    for (int m = 0; m < 32; ++m) {
-      if ((m & 7) == 0) asm volatile("" ::: "memory");
+    // acc += round(inverse transform), register m = coefficients lane + 32 m and lane + 32 m + M
+    dit_dft32_untwist_to<10 + 32, PNB_BR_CBANK>(x, [&](int m) {
       const int j = lane + 32 * m;
       uint2 o = acc2[j];
       o.x += top32_round(x[m].x);
       o.y += top32_round(x[m].y);
       acc2[j] = o;
-    }
+    });
     __syncwarp();
   }
   tc::tc_fence_before();
