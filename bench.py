@@ -56,6 +56,16 @@ PKG_DIR = os.path.join(ROOT, "penumbra-fhe_b200")
 
 SEED = 20241201
 FLOP_PER_PBS = 834 * (4 * 51200 + 32768)  # 1.981e8 FFT-equivalent FP64 flop (n=834, N=2048)
+
+
+def flop_per_pbs(n=834, N=2048, k=1, levels=1):
+    """FFT-equivalent FP64 flop of one bootstrap: n CMux steps of (k+1) l forward and k+1 inverse
+    transforms of N/2 complex points (5 (N/2) log2(N/2) each) and (k+1)^2 l pointwise complex
+    multiply-adds (8 flop each)."""
+    import math
+    h = N // 2
+    return n * (((k + 1) * levels + (k + 1)) * 5 * h * int(math.log2(h)) +
+                (k + 1) ** 2 * levels * h * 8)
 WORKLOAD = ("pbs_microbenchmark: n=834 k=1 N=2048 pbs=(2^23,1) ks=(2^3,5) gaussian noise, "
             "uniform 4-bit messages, random 16-entry LUT")
 # DRAM bytes (read + write) of one blind-rotation launch over 4096 ciphertexts: a one-pass ncu
@@ -375,9 +385,11 @@ def batch_sweep(pnb, keys, dev, flush, batches=(1, 16, 256, 1024, 4096, 16384, 6
     return out
 
 
-def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6), (5, 9)), B=4096):
+def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6), (5, 9)), B=4096,
+                fp64_peak=None):
     """PBS/s of the multi-level key sets the graph planner uses (keyswitch + blind rotation,
-    device-timed at batch B, L2 flushed between repetitions), each checked by decryption."""
+    device-timed at batch B, L2 flushed between repetitions), each checked by decryption, with
+    its FFT-equivalent FP64 rate against the FP64 peak measured in the run."""
     import numpy as np
     import torch
     rng = np.random.default_rng(SEED + 31)
@@ -411,7 +423,11 @@ def key_set_leg(pnb, dev, flush, sets=((15, 2), (11, 3), (10, 4), (7, 6), (5, 9)
             torch.cuda.synchronize(dev)
             ms += a.elapsed_time(b)
         ms /= reps
-        out.append({"key": [base_log, levels], "pbs_per_second": round(B / (ms * 1e-3)),
+        rate = B / (ms * 1e-3)
+        tflops = flop_per_pbs(levels=levels) * rate / 1e12
+        out.append({"key": [base_log, levels], "pbs_per_second": round(rate),
+                    "fp64_tflops": round(tflops, 2),
+                    "fp64_frac": round(tflops / fp64_peak, 3) if fp64_peak else None,
                     "decrypt_ok": ok, "log2_noise_std": round(log2_std, 3)})
         del ct, small, ks_ws, o
         keys.free()
@@ -834,9 +850,15 @@ def run_gpu(args):
                        args.noise_exact if world == 1 else 0)
              if (rank == 0 and args.noise) else None)
     sweep = batch_sweep(pnb, keys, dev, flush) if (rank == 0 and args.sweep) else None
-    key_sets = key_set_leg(pnb, dev, flush) if (rank == 0 and args.key_sets) else None
+    key_sets = (key_set_leg(pnb, dev, flush, fp64_peak=peak)
+                if (rank == 0 and args.key_sets) else None)
     n8k = (n8192_leg(args, pnb, world, rank, local, dist, dev, flush, comm)
            if args.n8k else None)
+    if n8k is not None:  # the N = 8192 bootstrap's FP64 rate against the same peak
+        pp = n8k["pbs"]
+        pp["fp64_tflops"] = round(flop_per_pbs(n=pp["params"]["n"], N=pp["params"]["N"]) *
+                                  pp["pbs_per_second"] / 1e12, 2)
+        pp["fp64_frac"] = round(pp["fp64_tflops"] / peak, 3)
     lin_rq = (None if args.lr_batch <= 0
               else linear_requant_leg(args, pnb, world, rank, local, dist, dev, comm))
     cnn = (None if args.cnn_batch <= 0

@@ -938,14 +938,16 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
     }
     if (aborted) break;
     fft_inverse_h<PNB_ML_CBANK, A32 ? 10 + 32 : 10 + 16>(x, buf, lane, tb.wi);
+    // acc += round(inverse transform): the 32-bit form by one 64-bit conversion (|w| < 2^63),
+    // the 48-bit form by three FP64 operations (|w| reaches past 2^63)
 #pragma unroll
     for (int m = 0; m < 32; ++m) {
       if ((m & 7) == 0) asm volatile("" ::: "memory");
       const int j = lane + 32 * m;
       if (A32) {
         uint2 h = hi2[j];
-        h.x += scaled_f64_to_top32(x[m].x);
-        h.y += scaled_f64_to_top32(x[m].y);
+        h.x += top32_round(x[m].x);
+        h.y += top32_round(x[m].y);
         hi2[j] = h;
       } else {
         const uint2 h = hi2[j];
