@@ -781,10 +781,27 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
   uint64_t a_next = valid ? in[0] : 0;  // mask coefficient of the next CMux, loaded one ahead
   __syncthreads();
 
-  // this warp's lane quarter and column range; column 4r + {0..3} holds spectrum row r
-  const uint32_t tfacc = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
-                         ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
-  const uint32_t tvk = tfacc + 256u;  // the level-0 pass's vk words, 128 columns further on
+  // this warp's lane quarter and column range; column 4r + {0..3} holds spectrum row r.  The
+  // 32-bit form keeps one vk word per coefficient (64 columns per warp), and the forward
+  // transform's twiddles T(r, lane) take the quarter's last 128 columns.
+  const uint32_t tq = *reinterpret_cast<volatile uint32_t*>(tmem_holder) +
+                      ((uint32_t)(32 * (warp & 3)) << 16);
+  const uint32_t tfacc = tq + (uint32_t)(128 * (warp >> 2));
+  const uint32_t tvk = A32 ? tq + 256u + (uint32_t)(64 * (warp >> 2)) : tfacc + 256u;
+  const uint32_t t_fwd = tq + 384u;
+  if (A32 && warp < 4) {  // one warp per lane quarter writes its twiddles
+#pragma unroll 1
+    for (int g = 0; g < 8; ++g) {
+      uint32_t t[16];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) d2_to_words(tb.wf[(4 * g + q) * 32 + lane], t + 4 * q);
+      tc::tmem_st_32x32_x16(t_fwd + 16u * g, t);
+    }
+    tc::tmem_st_wait();
+    tc::tc_fence_before();
+  }
+  __syncthreads();
+  tc::tc_fence_after();
   const double2* f_own = ggsw_s + (size_t)(p * 2 + p) * FFT_M;
   const double2* f_oth = ggsw_s + (size_t)((p ^ 1) * 2 + p) * FFT_M;
   // Gadget digits: with T = beta L and H = sum_j 2^(beta-1) 2^(beta j), the balanced digits of
@@ -817,7 +834,7 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
       const uint64_t flip = (a >= FFT_N) ? ~0ull : 0ull;
 #pragma unroll
       for (int g = 0; g < 8; ++g) {
-        uint32_t t[16];
+        uint32_t t[16], u[8];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int j = lane + 32 * (4 * g + q);
@@ -835,10 +852,8 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
             const uint32_t n0 = (tr < 0 ? ~0u : 0u) ^ f32, n1 = (tr < -FFT_M ? ~0u : 0u) ^ f32;
             const uint32_t g0 = sw ? gh.y : gh.x, g1 = sw ? gh.x : gh.y;
             const uint32_t w0 = ((g0 ^ n0) - n0) - oh.x, w1 = ((g1 ^ n1) - n1) - oh.y;
-            t[4 * q + 0] = 0u;
-            t[4 * q + 1] = w0 + off_h + ((w0 >> rnd_sh) & 1u);
-            t[4 * q + 2] = 0u;
-            t[4 * q + 3] = w1 + off_h + ((w1 >> rnd_sh) & 1u);
+            u[2 * q + 0] = w0 + off_h + ((w0 >> rnd_sh) & 1u);
+            u[2 * q + 1] = w1 + off_h + ((w1 >> rnd_sh) & 1u);
           } else {
             const ushort2 gl = lo2[tr & (FFT_M - 1)], ol = lo2[j];
             const uint64_t n0 = (tr < 0 ? ~0ull : 0ull) ^ flip;
@@ -853,7 +868,8 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
             t[4 * q + 3] = (uint32_t)(v1 >> 32);
           }
         }
-        tc::tmem_st_32x32_x16(tvk + (uint32_t)(16 * g), t);
+        if (A32) tc::tmem_st_32x32_x8(tvk + (uint32_t)(8 * g), u);
+        else tc::tmem_st_32x32_x16(tvk + (uint32_t)(16 * g), t);
       }
       tc::tmem_st_wait();
     }
@@ -862,20 +878,47 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
       // digit `lev` sits in bits [sh, sh + beta) of vk: a funnel shift by min(sh, 32), then sh - 32
       const int sh = 64 - beta * (lev + 1);
       const int sh_a = sh < 32 ? sh : 32, sh_b = sh - sh_a;
+      if (A32) {
 #pragma unroll
-      for (int g = 0; g < 8; ++g) {
-        uint32_t t[16];
-        tc::tmem_ld_32x32_x16(tvk + (uint32_t)(16 * g), t);
-        tc::tmem_ld_wait();
+        for (int g = 0; g < 8; ++g) {
+          uint32_t u[8];
+          tc::tmem_ld_32x32_x8(tvk + (uint32_t)(8 * g), u);
+          tc::tmem_ld_wait();
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const int d = (int)((__funnelshift_rc(t[2 * q], t[2 * q + 1], sh_a) >> sh_b) & dmask) -
-                        dhalf;
-          if (q & 1) x[4 * g + (q >> 1)].y = (double)d;
-          else x[4 * g + (q >> 1)].x = (double)d;
+          for (int q = 0; q < 8; ++q) {
+            const int d = (int)((u[q] >> (sh - 32)) & dmask) - dhalf;
+            if (q & 1) x[4 * g + (q >> 1)].y = (double)d;
+            else x[4 * g + (q >> 1)].x = (double)d;
+          }
         }
+        // forward transform with the mid twiddles from tensor memory
+        crt_dft32<32, PNB_ML_CBANK>(x);
+#pragma unroll
+        for (int g = 0; g < 32 / BR_TC; ++g) {
+          uint32_t t[4 * BR_TC];
+          tm_load8(t_fwd + 4u * BR_TC * g, t);
+#pragma unroll
+          for (int q = 0; q < BR_TC; ++q)
+            x[BR_TC * g + q] = cmul(x[BR_TC * g + q], words_to_d2(t + 4 * q));
+        }
+        warp_transpose_half(x, buf, lane);
+        crt_dft32<0, PNB_ML_CBANK>(x);
+      } else {
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          uint32_t t[16];
+          tc::tmem_ld_32x32_x16(tvk + (uint32_t)(16 * g), t);
+          tc::tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int d =
+                (int)((__funnelshift_rc(t[2 * q], t[2 * q + 1], sh_a) >> sh_b) & dmask) - dhalf;
+            if (q & 1) x[4 * g + (q >> 1)].y = (double)d;
+            else x[4 * g + (q >> 1)].x = (double)d;
+          }
+        }
+        fft_forward_h<PNB_ML_CBANK>(x, buf, lane, tb.wf);
       }
-      fft_forward_h<PNB_ML_CBANK>(x, buf, lane, tb.wf);
       // this level's key rows must have landed (bounded wait; parity = stage mod 2)
       if (!tc::mbar_wait(bar, stage & 1u, BR_WAIT_LIMIT)) {
         *abort_s = 1;
