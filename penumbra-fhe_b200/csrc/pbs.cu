@@ -931,36 +931,32 @@ __global__ void __launch_bounds__(64 * MLB_CPB, 1) blind_rotate_mlb_kernel(
         for (int rr = 0; rr < 16; ++rr) xch[rr * 32 + lane] = x[16 * h + rr];
         pair_sync(cl);
 #pragma unroll
-        for (int g4 = 0; g4 < 4; ++g4) {
-          const int rb = 16 * h + 4 * g4;  // four spectrum rows = 16 TMEM columns
-          uint32_t t[16];
+        for (int g8 = 0; g8 < 2; ++g8) {
+          const int rb = 16 * h + 8 * g8;  // eight spectrum rows = 32 TMEM columns
+          uint32_t t[32];
           if (lev > 0) {
-            tc::tmem_ld_32x32_x16(tfacc + (uint32_t)(4 * rb), t);
+            tc::tmem_ld_32x32_nowait(tfacc + (uint32_t)(4 * rb), t);
             tc::tmem_ld_wait();
           }
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
+          for (int q = 0; q < 8; ++q) {
             const int r = rb + q;
             const int e = r * 32 + lane;
             const double2 fo = f_own[e], ft = f_oth[e];
             const double2 dt = och[(r - 16 * h) * 32 + lane];
-            const double2 p0 = cmul(x[r], fo);
-            double2 v = make_double2(p0.x + fma(dt.x, ft.x, -dt.y * ft.y),
-                                     p0.y + fma(dt.x, ft.y, dt.y * ft.x));
-            if (lev > 0) {
-              v.x += __hiloint2double((int)t[4 * q + 1], (int)t[4 * q + 0]);
-              v.y += __hiloint2double((int)t[4 * q + 3], (int)t[4 * q + 2]);
-            }
+            // x fo + dt ft (+ the earlier levels' sum) as one chain of fused multiply-adds
+            const double2 sum = lev > 0 ? words_to_d2(t + 4 * q) : make_double2(0.0, 0.0);
+            const double2 xv = x[r];
+            const double2 v =
+                make_double2(fma(xv.x, fo.x, fma(-xv.y, fo.y, fma(dt.x, ft.x, fma(-dt.y, ft.y, sum.x)))),
+                             fma(xv.x, fo.y, fma(xv.y, fo.x, fma(dt.x, ft.y, fma(dt.y, ft.x, sum.y)))));
             if (last) {
               x[r] = v;
             } else {
-              t[4 * q + 0] = (uint32_t)__double2loint(v.x);
-              t[4 * q + 1] = (uint32_t)__double2hiint(v.x);
-              t[4 * q + 2] = (uint32_t)__double2loint(v.y);
-              t[4 * q + 3] = (uint32_t)__double2hiint(v.y);
+              d2_to_words(v, t + 4 * q);
             }
           }
-          if (!last) tc::tmem_st_32x32_x16(tfacc + (uint32_t)(4 * rb), t);
+          if (!last) tc::tmem_st_32x32(tfacc + (uint32_t)(4 * rb), t);
         }
         pair_sync(cl);
       }
