@@ -590,9 +590,12 @@ __global__ void __launch_bounds__(T8, 1) blind_rotate8k_kernel(
         for (int q4 = 0; q4 < 4; ++q4) {
           const int q = 4 * c + q4;
           const double2 f0 = f[q4 * T8 + v], f1 = f[4 * T8 + q4 * T8 + v];
-          const double2 a0 = cmul(x[q], f0), a1 = cmul(x[q], f1);
-          o0[q].x += a0.x; o0[q].y += a0.y;
-          o1[q].x += a1.x; o1[q].y += a1.y;
+          // o += x f as two fused multiply-adds per component
+          const double2 xv = x[q];
+          o0[q] = make_double2(fma(xv.x, f0.x, fma(-xv.y, f0.y, o0[q].x)),
+                               fma(xv.x, f0.y, fma(xv.y, f0.x, o0[q].y)));
+          o1[q] = make_double2(fma(xv.x, f1.x, fma(-xv.y, f1.y, o1[q].x)),
+                               fma(xv.x, f1.y, fma(xv.y, f1.x, o1[q].y)));
         }
         __syncwarp();
         if (lane == 0) tc::mbar_arrive(empty0 + 8u * st);
