@@ -78,10 +78,10 @@ std::vector<KeyLevel> default_levels(int n, int N, int k, double glwe_std) {
     double sig, cost;
   };
   // noise measured on a B200 over 4096 bootstraps (rounded up); cost = measured time per
-  // bootstrap relative to the single-level kernel (87.7k PBS/s against 44.1k, 28.7k, 23.1k,
-  // 16.5k and 11.6k at batch 4096)
-  static const Row rows[] = {{23, 1, 49.1, 1.0}, {15, 2, 42.0, 1.99}, {11, 3, 38.75, 3.06},
-                             {10, 4, 36.6, 3.80}, {7, 6, 33.9, 5.30}, {5, 9, 32.3, 7.56}};
+  // bootstrap relative to the single-level kernel (87.6k PBS/s against 44.6k, 29.4k, 23.7k,
+  // 17.0k and 12.0k at batch 4096)
+  static const Row rows[] = {{23, 1, 49.1, 1.0}, {15, 2, 42.0, 1.96}, {11, 3, 38.75, 2.98},
+                             {10, 4, 36.6, 3.70}, {7, 6, 33.9, 5.15}, {5, 9, 32.3, 7.33}};
   const bool is_default = (n == 834 && N == 2048 && k == 1 &&
                            std::fabs(glwe_std - 2.845267479601915e-15) < 1e-20);
   std::vector<KeyLevel> out;
